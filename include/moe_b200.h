@@ -1,0 +1,139 @@
+/*
+ * moe_b200.h - C ABI of the B200 (sm_100a) fused FP8 block-scale MoE forward.
+ *
+ * Drop-in for the hot path of nikhilnd/mlsys26-flashinfer-moe, whose whole
+ * product is the Python entry point
+ *
+ *   run(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+ *       gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+ *       local_expert_offset, routed_scaling_factor, output)      (kernel.py:562-575)
+ *
+ * The reference has no native library; these entry points are what its
+ * Triton launches (kernel.py:624-729) become when they are bound through a
+ * plain C interface (ctypes / cffi / any FFI).  Signatures hold only plain
+ * pointers, sizes and a cudaStream_t passed as void*: no framework types.
+ *
+ * Layouts (all row-major, e4m3 = OCP float8 e4m3fn stored as bytes):
+ *   routing_logits      [T, E_global]              fp32
+ *   routing_bias        [E_global]                 fp32 / bf16 / fp16 (bias_dtype)
+ *   hidden_states       [T, H]                     e4m3
+ *   hidden_states_scale [H/128, T]                 fp32 (token-minor, kernel.py:603)
+ *   gemm1_weights       [E_local, 2*I, H]          e4m3 (rows [0,I) multiply, [I,2I) gate the SiLU)
+ *   gemm1_weights_scale [E_local, 2*I/128, H/128]  fp32
+ *   gemm2_weights       [E_local, H, I]            e4m3
+ *   gemm2_weights_scale [E_local, H/128, I/128]    fp32
+ *   output              [T, H]                     bf16
+ *
+ * Every call is asynchronous on `stream`, performs no host<->device
+ * synchronisation and allocates nothing: scratch lives in the caller's
+ * workspace (see moe_fp8_workspace_size).
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (0 = success).  The Python layer maps shape/dtype errors to
+ * AssertionError (reference kernel.py:591-607) and the rest to RuntimeError. */
+#define MOE_OK 0
+#define MOE_ERR_INVALID_ARG (-1)     /* null pointer or bad enum value */
+#define MOE_ERR_SHAPE (-2)           /* unsupported or inconsistent shape */
+#define MOE_ERR_ALIGNMENT (-3)       /* a pointer is not 16-byte aligned */
+#define MOE_ERR_WORKSPACE (-4)       /* workspace missing or too small */
+#define MOE_ERR_CUDA (-5)            /* a CUDA runtime / driver call failed */
+#define MOE_ERR_TIMEOUT (-6)         /* a device-side bounded wait expired */
+#define MOE_ERR_DEVICE (-7)          /* device is not sm_100 */
+
+/* routing_bias element type */
+#define MOE_BIAS_F32 0
+#define MOE_BIAS_BF16 1
+#define MOE_BIAS_F16 2
+
+typedef struct MoeFwdArgs {
+  const float* routing_logits;
+  const void* routing_bias;
+  const void* hidden_states;
+  const float* hidden_states_scale;
+  const void* gemm1_weights;
+  const float* gemm1_weights_scale;
+  const void* gemm2_weights;
+  const float* gemm2_weights_scale;
+  void* output;
+  int64_t T;                   /* tokens (may be 0) */
+  int64_t H;                   /* hidden size, multiple of 256 */
+  int64_t I;                   /* intermediate size, multiple of 128 */
+  int64_t E_global;            /* routed experts, <= 256 */
+  int64_t E_local;             /* experts with weights here, <= E_global */
+  int64_t local_expert_offset; /* first local expert (reference kernel.py:572) */
+  int64_t n_group;             /* expert groups (8 for DeepSeek-V3) */
+  int64_t topk_group;          /* groups kept per token (4) */
+  int64_t top_k;               /* experts per token (8), <= 8 */
+  float routed_scaling_factor;
+  int32_t bias_dtype;          /* MOE_BIAS_* */
+  void* workspace;             /* device scratch, 256-byte aligned */
+  size_t workspace_bytes;
+} MoeFwdArgs;
+
+/* Offsets (bytes from the workspace base) of the per-stage buffers a forward
+ * leaves behind; tests read them to check each stage on its own.  npad is the
+ * row capacity of the expert-contiguous (permuted) buffers. */
+typedef struct MoeWorkspaceLayout {
+  size_t total_bytes;
+  int64_t npad;            /* rows of the permuted buffers (multiple of 128) */
+  int64_t route_blocks;    /* blocks of the routing kernel */
+  int64_t tokens_per_block;
+  size_t ctrl;             /* control block: done counter, device error code */
+  size_t topk_idx;         /* [T, top_k] int32   routed global expert ids, selection order */
+  size_t topk_weights;     /* [T, top_k] fp32    routing weights */
+  size_t block_base;       /* [route_blocks, E_local] int32 per-block bucket offsets */
+  size_t counts;           /* [E_local] int32    assignments per local expert */
+  size_t tile_start;       /* [E_local + 1] int32 prefix sum of 128-row tiles */
+  size_t row_token;        /* [npad] int32       token of each permuted row */
+  size_t row_weight;       /* [npad] fp32        routing weight of each permuted row */
+  size_t a_perm;           /* [npad, H] e4m3     permuted hidden states */
+  size_t a_scale_perm;     /* [H/128, npad] fp32 their scales */
+  size_t inter;            /* [npad, I] e4m3     SwiGLU output, requantised */
+  size_t inter_scale;      /* [I/64, npad] fp32  its per-64-column scales */
+  size_t out_f32;          /* [T, H] fp32        scatter-add accumulator */
+} MoeWorkspaceLayout;
+
+/* Workspace bytes needed for the shape in `a` (pointers are not read).
+ * Replaces the torch allocations of kernel.py:629-630, 348, 358, 364-368,
+ * 664-670 and 704. */
+int moe_fp8_workspace_size(const MoeFwdArgs* a, size_t* bytes);
+
+/* Byte offsets of the stage buffers inside the workspace. */
+int moe_fp8_workspace_layout(const MoeFwdArgs* a, MoeWorkspaceLayout* out);
+
+/* The whole layer: routing -> dispatch -> GEMM1+SwiGLU+requant -> GEMM2 with
+ * weighted scatter-add -> bf16 output.  Replaces run() (kernel.py:562-729).
+ * Only experts [local_expert_offset, local_expert_offset + E_local) contribute;
+ * tokens routed elsewhere get zeros, as in the reference. */
+int moe_fp8_forward(const MoeFwdArgs* a, void* stream);
+
+/* Routing only: writes topk_idx / topk_weights (and the dispatch counters) in
+ * the workspace.  Replaces moe_routing_kernel (kernel.py:428-542) plus the
+ * counting pass of build_expert_dispatch (kernel.py:252-285, 327-361). */
+int moe_fp8_route(const MoeFwdArgs* a, void* stream);
+
+/* Device-side error word of the last forward on this workspace (0 = none).
+ * Reads the control block with a blocking copy on `stream`. */
+int moe_fp8_device_error(const MoeFwdArgs* a, void* stream, int32_t* code, int32_t* info);
+
+/* Human-readable name of a status code. */
+const char* moe_fp8_status_string(int code);
+
+/* Number of streaming multiprocessors the persistent kernels size their grid
+ * to (queried once per device). */
+int moe_fp8_num_sms(int device, int32_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

@@ -1,0 +1,396 @@
+// C ABI of the fused FP8 MoE forward: argument validation, workspace layout,
+// TMA descriptor construction and the launch sequence.  No allocation and no
+// host<->device synchronisation happen on the forward path.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "moe_kernels.cuh"
+
+namespace moe {
+namespace {
+
+constexpr int kLayoutSms = 148;   // token-per-block heuristic (B200 SM count)
+constexpr size_t kAlign = 1024;
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+bool is_pow2(int64_t x) { return x > 0 && (x & (x - 1)) == 0; }
+
+// Shape rules, mirroring the reference's asserts (kernel.py:591-607) but
+// generalised to any layer this kernel family supports.
+int validate_shape(const MoeFwdArgs* a) {
+  if (a->T < 0 || a->T > (int64_t(1) << 28)) return MOE_ERR_SHAPE;
+  if (a->H < 256 || a->H % 256 != 0 || a->H > 65536) return MOE_ERR_SHAPE;
+  if (a->I < 128 || a->I % 128 != 0 || a->I > 65536) return MOE_ERR_SHAPE;
+  const int64_t e = a->E_global;
+  if (e < 1 || e > kMaxExperts) return MOE_ERR_SHAPE;
+  if (a->n_group < 1 || e % a->n_group != 0) return MOE_ERR_SHAPE;
+  const int64_t g = e / a->n_group;
+  const int64_t epl = e <= 32 ? 1 : e / 32;
+  if (e > 32 && e % 32 != 0) return MOE_ERR_SHAPE;
+  if (!is_pow2(epl) || epl > 8 || g % epl != 0 || !is_pow2(g / epl)) return MOE_ERR_SHAPE;
+  if (a->topk_group < 1 || a->topk_group > a->n_group) return MOE_ERR_SHAPE;
+  if (a->top_k < 1 || a->top_k > kMaxTopK || a->top_k > a->topk_group * g) return MOE_ERR_SHAPE;
+  if (a->E_local < 1 || a->E_local > e) return MOE_ERR_SHAPE;
+  if (a->local_expert_offset < 0 || a->local_expert_offset + a->E_local > e) return MOE_ERR_SHAPE;
+  if (a->bias_dtype != MOE_BIAS_F32 && a->bias_dtype != MOE_BIAS_BF16 &&
+      a->bias_dtype != MOE_BIAS_F16)
+    return MOE_ERR_INVALID_ARG;
+  return MOE_OK;
+}
+
+struct Layout {
+  MoeWorkspaceLayout w;
+  int tokens_per_block;
+  int blocks;
+};
+
+Layout make_layout(const MoeFwdArgs* a) {
+  Layout L{};
+  const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local, K = a->top_k;
+  int64_t tpw = (T + kLayoutSms * 8 - 1) / (kLayoutSms * 8);
+  if (tpw < 1) tpw = 1;
+  int64_t tpb = 8 * tpw;
+  if (tpb > kMaxTokensPerBlock) tpb = kMaxTokensPerBlock;
+  L.tokens_per_block = static_cast<int>(tpb);
+  L.blocks = static_cast<int>((T + tpb - 1) / tpb);
+  const int64_t nmax = T * (K < El ? K : El);
+  const int64_t active = El < nmax ? El : nmax;
+  int64_t tiles = (nmax + active * (kTileM - 1)) / kTileM;
+  if (tiles < 1) tiles = 1;
+  const int64_t npad = tiles * kTileM;
+  MoeWorkspaceLayout& w = L.w;
+  w.npad = npad;
+  w.route_blocks = L.blocks;
+  w.tokens_per_block = tpb;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, kAlign);
+    return at;
+  };
+  w.ctrl = take(sizeof(CtrlBlock));
+  w.topk_idx = take(sizeof(int) * T * K);
+  w.topk_weights = take(sizeof(float) * T * K);
+  w.block_base = take(sizeof(int) * (L.blocks > 0 ? L.blocks : 1) * El);
+  w.counts = take(sizeof(int) * El);
+  w.tile_start = take(sizeof(int) * (El + 1));
+  w.row_token = take(sizeof(int) * npad);
+  w.row_weight = take(sizeof(float) * npad);
+  w.a_perm = take(static_cast<size_t>(npad) * H);
+  w.a_scale_perm = take(sizeof(float) * (H / kBlockK) * npad);
+  w.inter = take(static_cast<size_t>(npad) * I);
+  w.inter_scale = take(sizeof(float) * (I / kInterScaleBlock) * npad);
+  w.out_f32 = take(sizeof(float) * T * H);
+  w.total_bytes = off;
+  return L;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// device properties and TMA descriptors
+// ---------------------------------------------------------------------------
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  bool attrs_set = false;
+};
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOE_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return MOE_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return MOE_ERR_CUDA;
+  }
+  if (d.major != 10) return MOE_ERR_DEVICE;
+  if (!d.attrs_set) {
+    if (gemm_set_smem_attrs() != MOE_OK) return MOE_ERR_CUDA;
+    d.attrs_set = true;
+  }
+  *out = &d;
+  return MOE_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Byte matrix [rows, cols] (row stride = cols) read in 128x128 boxes with the
+// 128-byte swizzle the UMMA descriptors expect.
+struct MapKey {
+  const void* base;
+  uint64_t cols, rows;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && cols == o.cols && rows == o.rows;
+  }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool used;
+};
+constexpr int kMapCache = 64;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+
+int byte_tile_map(const void* base, uint64_t cols, uint64_t rows, CUtensorMap* out) {
+  const MapKey key{base, cols, rows};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (int i = 0; i < kMapCache; ++i)
+      if (g_maps[i].used && g_maps[i].key == key) {
+        *out = g_maps[i].map;
+        return MOE_OK;
+      }
+  }
+  auto fn = encode_fn();
+  if (!fn) return MOE_ERR_CUDA;
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(kTileM)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return MOE_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_maps[g_map_next] = MapEntry{key, m, true};
+    g_map_next = (g_map_next + 1) % kMapCache;
+  }
+  *out = m;
+  return MOE_OK;
+}
+
+int check_args(const MoeFwdArgs* a, Layout* L) {
+  if (!a) return MOE_ERR_INVALID_ARG;
+  int st = validate_shape(a);
+  if (st) return st;
+  *L = make_layout(a);
+  if (a->T == 0) return MOE_OK;
+  if (!a->routing_logits || !a->routing_bias || !a->hidden_states || !a->hidden_states_scale ||
+      !a->gemm1_weights || !a->gemm1_weights_scale || !a->gemm2_weights ||
+      !a->gemm2_weights_scale || !a->output)
+    return MOE_ERR_INVALID_ARG;
+  if (!a->workspace || a->workspace_bytes < L->w.total_bytes) return MOE_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return MOE_ERR_ALIGNMENT;
+  if (!aligned16(a->hidden_states) || !aligned16(a->gemm1_weights) ||
+      !aligned16(a->gemm2_weights) || !aligned16(a->output) || !aligned16(a->routing_logits))
+    return MOE_ERR_ALIGNMENT;
+  return MOE_OK;
+}
+
+template <class T>
+T* ws_ptr(const MoeFwdArgs* a, size_t off) {
+  return reinterpret_cast<T*>(static_cast<uint8_t*>(a->workspace) + off);
+}
+
+int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
+  const MoeWorkspaceLayout& w = L.w;
+  RouteParams rp{};
+  rp.logits = a->routing_logits;
+  rp.bias = a->routing_bias;
+  rp.bias_dtype = a->bias_dtype;
+  rp.T = static_cast<int>(a->T);
+  rp.E = static_cast<int>(a->E_global);
+  rp.n_group = static_cast<int>(a->n_group);
+  rp.topk_group = static_cast<int>(a->topk_group);
+  rp.top_k = static_cast<int>(a->top_k);
+  const int epl = rp.E <= 32 ? 1 : rp.E / 32;
+  rp.experts_per_lane = epl;
+  rp.lanes_per_group = (rp.E / rp.n_group) / epl;
+  rp.E_local = static_cast<int>(a->E_local);
+  rp.local_expert_offset = static_cast<int>(a->local_expert_offset);
+  rp.routed_scaling_factor = a->routed_scaling_factor;
+  rp.tokens_per_block = L.tokens_per_block;
+  rp.topk_idx = ws_ptr<int>(a, w.topk_idx);
+  rp.topk_weights = ws_ptr<float>(a, w.topk_weights);
+  rp.block_base = ws_ptr<int>(a, w.block_base);
+  rp.counts = ws_ptr<int>(a, w.counts);
+  rp.tile_start = ws_ptr<int>(a, w.tile_start);
+  rp.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
+  if (cudaMemsetAsync(rp.ctrl, 0, sizeof(CtrlBlock), s) != cudaSuccess) return MOE_ERR_CUDA;
+  moe_route_kernel<<<L.blocks, kRouteThreads, 0, s>>>(rp);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
+  DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st) return st;
+  const MoeWorkspaceLayout& w = L.w;
+  const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local;
+  float* out_f32 = ws_ptr<float>(a, w.out_f32);
+  if (cudaMemsetAsync(out_f32, 0, sizeof(float) * T * H, s) != cudaSuccess) return MOE_ERR_CUDA;
+  st = launch_route(a, L, s);
+  if (st) return st;
+
+  PermuteParams pp{};
+  pp.T = static_cast<int>(T);
+  pp.H = static_cast<int>(H);
+  pp.top_k = static_cast<int>(a->top_k);
+  pp.E_local = static_cast<int>(El);
+  pp.local_expert_offset = static_cast<int>(a->local_expert_offset);
+  pp.tokens_per_block = L.tokens_per_block;
+  pp.npad = w.npad;
+  pp.topk_idx = ws_ptr<int>(a, w.topk_idx);
+  pp.topk_weights = ws_ptr<float>(a, w.topk_weights);
+  pp.block_base = ws_ptr<int>(a, w.block_base);
+  pp.tile_start = ws_ptr<int>(a, w.tile_start);
+  pp.hidden = static_cast<const uint8_t*>(a->hidden_states);
+  pp.hs_scale = a->hidden_states_scale;
+  pp.row_token = ws_ptr<int>(a, w.row_token);
+  pp.row_weight = ws_ptr<float>(a, w.row_weight);
+  pp.a_perm = ws_ptr<uint8_t>(a, w.a_perm);
+  pp.a_scale_perm = ws_ptr<float>(a, w.a_scale_perm);
+  moe_permute_kernel<<<L.blocks, kRouteThreads, 0, s>>>(pp);
+  if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+
+  CUtensorMap tm_a1, tm_b1, tm_a2, tm_b2;
+  if ((st = byte_tile_map(pp.a_perm, H, w.npad, &tm_a1))) return st;
+  if ((st = byte_tile_map(a->gemm1_weights, H, El * 2 * I, &tm_b1))) return st;
+  if ((st = byte_tile_map(ws_ptr<uint8_t>(a, w.inter), I, w.npad, &tm_a2))) return st;
+  if ((st = byte_tile_map(a->gemm2_weights, I, El * H, &tm_b2))) return st;
+
+  GemmParams g1{};
+  g1.tile_start = pp.tile_start;
+  g1.counts = ws_ptr<int>(a, w.counts);
+  g1.E_local = static_cast<int>(El);
+  g1.num_k_blocks = static_cast<int>(H / kBlockK);
+  g1.n_tiles = static_cast<int>(I / (kTileN / 2));
+  g1.b_rows_per_expert = static_cast<int>(2 * I);
+  g1.inter = static_cast<int>(I);
+  g1.hidden = static_cast<int>(H);
+  g1.npad = w.npad;
+  g1.a_scale = pp.a_scale_perm;
+  g1.b_scale = a->gemm1_weights_scale;
+  g1.inter_out = ws_ptr<uint8_t>(a, w.inter);
+  g1.inter_scale = ws_ptr<float>(a, w.inter_scale);
+  g1.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
+  if ((st = launch_gemm(kGemm1, tm_a1, tm_b1, g1, dev->sms, s))) return st;
+
+  GemmParams g2 = g1;
+  g2.num_k_blocks = static_cast<int>(I / kBlockK);
+  g2.n_tiles = static_cast<int>(H / kTileN);
+  g2.b_rows_per_expert = static_cast<int>(H);
+  g2.a_scale = g1.inter_scale;
+  g2.b_scale = a->gemm2_weights_scale;
+  g2.inter_out = nullptr;
+  g2.inter_scale = nullptr;
+  g2.row_token = pp.row_token;
+  g2.row_weight = pp.row_weight;
+  g2.out_f32 = out_f32;
+  if ((st = launch_gemm(kGemm2, tm_a2, tm_b2, g2, dev->sms, s))) return st;
+
+  const int64_t n8 = T * H / 8;
+  int blocks = static_cast<int>((n8 + 255) / 256);
+  if (blocks > dev->sms * 8) blocks = dev->sms * 8;
+  moe_finalize_kernel<<<blocks, 256, 0, s>>>(out_f32, static_cast<__nv_bfloat16*>(a->output), n8);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" {
+
+int moe_fp8_workspace_size(const MoeFwdArgs* a, size_t* bytes) {
+  if (!a || !bytes) return MOE_ERR_INVALID_ARG;
+  const int st = validate_shape(a);
+  if (st) return st;
+  *bytes = make_layout(a).w.total_bytes;
+  return MOE_OK;
+}
+
+int moe_fp8_workspace_layout(const MoeFwdArgs* a, MoeWorkspaceLayout* out) {
+  if (!a || !out) return MOE_ERR_INVALID_ARG;
+  const int st = validate_shape(a);
+  if (st) return st;
+  *out = make_layout(a).w;
+  return MOE_OK;
+}
+
+int moe_fp8_forward(const MoeFwdArgs* a, void* stream) {
+  Layout L;
+  int st = check_args(a, &L);
+  if (st) return st;
+  if (a->T == 0) return MOE_OK;
+  return launch_forward(a, L, static_cast<cudaStream_t>(stream));
+}
+
+int moe_fp8_route(const MoeFwdArgs* a, void* stream) {
+  Layout L;
+  int st = check_args(a, &L);
+  if (st) return st;
+  if (a->T == 0) return MOE_OK;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev))) return st;
+  return launch_route(a, L, static_cast<cudaStream_t>(stream));
+}
+
+int moe_fp8_device_error(const MoeFwdArgs* a, void* stream, int32_t* code, int32_t* info) {
+  Layout L;
+  if (!a || !code || !info) return MOE_ERR_INVALID_ARG;
+  int st = validate_shape(a);
+  if (st) return st;
+  L = make_layout(a);
+  if (!a->workspace || a->workspace_bytes < L.w.total_bytes) return MOE_ERR_WORKSPACE;
+  CtrlBlock host;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(&host, ws_ptr<CtrlBlock>(a, L.w.ctrl), sizeof(host), cudaMemcpyDeviceToHost,
+                      s) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return MOE_ERR_CUDA;
+  *code = host.error;
+  *info = host.error_info;
+  return MOE_OK;
+}
+
+const char* moe_fp8_status_string(int code) {
+  switch (code) {
+    case MOE_OK: return "ok";
+    case MOE_ERR_INVALID_ARG: return "invalid argument";
+    case MOE_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case MOE_ERR_ALIGNMENT: return "pointer not 16-byte aligned";
+    case MOE_ERR_WORKSPACE: return "workspace missing or too small";
+    case MOE_ERR_CUDA: return "CUDA call failed";
+    case MOE_ERR_TIMEOUT: return "device-side wait timed out";
+    case MOE_ERR_DEVICE: return "device is not sm_100 (B200)";
+    default: return "unknown status";
+  }
+}
+
+int moe_fp8_num_sms(int device, int32_t* out) {
+  if (!out) return MOE_ERR_INVALID_ARG;
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  *out = v;
+  return MOE_OK;
+}
+
+}  // extern "C"

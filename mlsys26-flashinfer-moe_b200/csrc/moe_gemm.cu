@@ -1,0 +1,360 @@
+// Persistent warp-specialised grouped GEMMs of the MoE forward on tcgen05.
+//
+// One CTA per SM walks a static list of work units (expert tile of 128
+// permuted rows x 256 output columns).  Roles:
+//   Warpgroup 2 (warps 8-11) gives registers to warpgroups 0-1 with setmaxnreg.
+//   warp 8  (one thread)  TMA producer: A tile 128x128 and B tile 256x128 (two
+//                         128-row boxes) per 128-deep K block, 4-stage ring.
+//   warp 9  (one thread)  MMA issuer: tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 ->
+//                         fp32), M=128 N=256 K=32, into one of two 256-column
+//                         TMEM partial accumulators.
+//   warps 0-7             Block-scale promotion and epilogue.  FP8 operands
+//                         carry one fp32 scale per 128 (A, W) or 64 (the
+//                         intermediate) K elements, which the tensor core
+//                         cannot apply, so every partial accumulator covers
+//                         exactly one scale block and is folded into fp32
+//                         registers as acc += partial * (sa[row] * sw[block]).
+//                         Warp w reads TMEM lanes 32*(w%4).. and column half
+//                         w/4, so each thread owns one row and 128 columns.
+//
+// kGemm1 (reference moe_gemm1_kernel, kernel.py:7-151): B rows are the gate
+//   half W1[e, n*128 : n*128+128] (multiplied, X1) followed by the SiLU half
+//   W1[e, I + n*128 : ...] (X2); epilogue C = silu(X2) * X1, per-row amax over
+//   64 columns, scale = max(amax/448, 1e-12), C/scale -> e4m3.
+// kGemm2 (reference moe_gemm2_kernel, kernel.py:153-250): B rows are
+//   W2[e, n*256 : n*256+256]; epilogue multiplies by the routing weight and
+//   does an fp32 vector reduction into out[token] (kernel.py:236-250).
+#include "moe_kernels.cuh"
+
+namespace moe {
+
+namespace {
+
+struct Unit {
+  int e, m, n, row0, nrows;
+};
+
+// Unit u -> (expert, tile of the expert, N tile).  Experts own the contiguous
+// unit range [tile_start[e]*NT, tile_start[e+1]*NT); inside it the N tile is
+// the outer index so the expert's row tiles reuse each weight tile from L2.
+__device__ __forceinline__ Unit decode_unit(int u, const int* tstart, const int* counts, int E,
+                                            int NT) {
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tstart[mid] * NT <= u) lo = mid;
+    else hi = mid - 1;
+  }
+  Unit c;
+  c.e = lo;
+  const int mt = tstart[lo + 1] - tstart[lo];
+  const int l = u - tstart[lo] * NT;
+  c.n = l / mt;
+  c.m = l - c.n * mt;
+  c.row0 = (tstart[lo] + c.m) * kTileM;
+  c.nrows = min(kTileM, counts[lo] - c.m * kTileM);
+  return c;
+}
+
+// Bounded wait that ignores the abort flag: used only to let copies and MMAs
+// already in flight land before the CTA releases its shared memory and TMEM.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) return;
+  }
+}
+
+}  // namespace
+
+template <int kMode>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
+                    const __grid_constant__ CUtensorMap tm_b, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * kStageABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kStageBBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* tstart_s = reinterpret_cast<int*>(tmem_slot + 2);
+  int* counts_s = tstart_s + kMaxExperts + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = p.E_local, NT = p.n_tiles, KB = p.num_k_blocks;
+
+  for (int i = threadIdx.x; i <= E; i += kGemmThreads) tstart_s[i] = p.tile_start[i];
+  for (int i = threadIdx.x; i < E; i += kGemmThreads) counts_s[i] = p.counts[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_units = tstart_s[E] * NT;
+
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;              // bit s: stage s has a load in flight
+      uint32_t issued_phase = 0;        // bit s: phase of that load
+      for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+        const Unit c = decode_unit(u, tstart_s, counts_s, E, NT);
+        const int b_row0 = c.e * p.b_rows_per_expert +
+                           (kMode == kGemm1 ? c.n * (kTileN / 2) : c.n * kTileN);
+        const int b_row1 = kMode == kGemm1 ? b_row0 + p.inter : b_row0 + kTileN / 2;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 1)) goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          uint8_t* a_dst = sA + stage * kStageABytes;
+          uint8_t* b_dst = sB + stage * kStageBBytes;
+          tma_load_2d(a_dst, &tm_a, &full[stage], kb * kBlockK, c.row0);
+          tma_load_2d(b_dst, &tm_b, &full[stage], kb * kBlockK, b_row0);
+          tma_load_2d(b_dst + kStageBBytes / 2, &tm_b, &full[stage], kb * kBlockK, b_row1);
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      if (*abort_flag) {
+        for (int s = 0; s < kStages; ++s)
+          if (issued & (1u << s)) drain_wait(&full[s], (issued_phase >> s) & 1u);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr int kGroups = kMode == kGemm1 ? 1 : 2;   // scale blocks per K block
+      constexpr int kMmaPerGroup = (kBlockK / 32) / kGroups;
+      const uint32_t idesc = umma_idesc_e4m3_f32(kTileM, kTileN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t g = 0;
+      for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.ctrl, 2)) goto mma_done;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * kStageABytes);
+          const uint32_t b_base = smem_u32(sB + stage * kStageBBytes);
+#pragma unroll
+          for (int gi = 0; gi < kGroups; ++gi) {
+            const uint32_t buf = g & 1u;
+            if (!mbar_wait(&tempty[buf], ((g >> 1) & 1u) ^ 1u, abort_flag, p.ctrl, 3))
+              goto mma_done;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kMmaPerGroup; ++kk) {
+              const uint32_t koff = static_cast<uint32_t>((gi * kMmaPerGroup + kk) * 32);
+              umma_f8(tmem_base + buf * kTileN, umma_desc_sw128(a_base + koff),
+                      umma_desc_sw128(b_base + koff), idesc, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(&tfull[buf]);
+            ++g;
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    mma_done:
+      // Every commit above arrives in order; once this one lands, all MMAs and
+      // their barrier arrivals are done and TMEM / smem can be released.
+      umma_commit(drain);
+      drain_wait(drain, 0);
+    }
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kEpilogueRegs));
+    // ------------------------------------------------------------ promotion + epilogue
+    const int q = warp & 3, h = warp >> 2;
+    const int r = q * 32 + lane;
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    const int kb_rows = p.hidden / kBlockK;          // H/128
+    const int ib_rows = p.inter / kBlockK;           // I/128
+    uint32_t g = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+      const Unit c = decode_unit(u, tstart_s, counts_s, E, NT);
+      const bool warp_active = q * 32 < c.nrows;
+      const bool row_valid = r < c.nrows;
+      const int64_t grow = static_cast<int64_t>(c.row0) + r;
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+
+      if constexpr (kMode == kGemm1) {
+        // W1 scale [E, 2I/128, H/128]: gate block n, SiLU block I/128 + n.
+        const float* ws = p.b_scale + static_cast<int64_t>(c.e) * (2 * ib_rows) * KB;
+        const float* ws_x1 = ws + static_cast<int64_t>(c.n) * KB;
+        const float* ws_x2 = ws + static_cast<int64_t>(ib_rows + c.n) * KB;
+        float sa_next = warp_active ? __ldg(p.a_scale + grow) : 0.f;
+        for (int kb = 0; kb < KB; ++kb) {
+          const float sa = sa_next;
+          if (warp_active && kb + 1 < KB)
+            sa_next = __ldg(p.a_scale + static_cast<int64_t>(kb + 1) * p.npad + grow);
+          const float s1 = sa * __ldg(ws_x1 + kb);
+          const float s2 = sa * __ldg(ws_x2 + kb);
+          const uint32_t buf = g & 1u;
+          if (!mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 4)) goto epi_done;
+          tc_fence_after();
+          if (warp_active) {
+            const uint32_t tb = t_lane + buf * kTileN;
+            float v[32];
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+              // chunks 0,1: X1 columns 64h..64h+63; chunks 2,3: X2 columns 128+64h..
+              const uint32_t col = (ch < 2 ? 0u : 128u) + 64u * h + 32u * (ch & 1);
+              tmem_ld32(tb + col, v);
+              tmem_ld_wait();
+              const float s = ch < 2 ? s1 : s2;
+#pragma unroll
+              for (int j = 0; j < 32; j += 2)
+                ffma2(acc[ch * 32 + j], acc[ch * 32 + j + 1], v[j], v[j + 1], s);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+          ++g;
+        }
+        // SwiGLU + 1x64 requant (kernel.py:128-151)
+        if (warp_active) {
+          float amax = 0.f;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const float x1 = acc[j], x2 = acc[64 + j];
+            const float cval = (x2 / (1.0f + expf(-x2))) * x1;
+            acc[j] = cval;
+            amax = fmaxf(amax, fabsf(cval));
+          }
+          const float sc = fmaxf(amax / 448.0f, 1e-12f);
+          if (row_valid) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t lo = pack_e4m3x2(acc[4 * j] / sc, acc[4 * j + 1] / sc);
+              const uint32_t hi = pack_e4m3x2(acc[4 * j + 2] / sc, acc[4 * j + 3] / sc);
+              packed[j] = lo | (hi << 16);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(p.inter_out + grow * p.inter + c.n * (kTileN / 2) +
+                                                  64 * h);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                                  packed[4 * j + 3]);
+            p.inter_scale[static_cast<int64_t>(2 * c.n + h) * p.npad + grow] = sc;
+          }
+        }
+      } else {
+        // W2 scale [E, H/128, I/128]: row block 2n + h of this thread's columns.
+        const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * kb_rows + 2 * c.n + h) * KB;
+        float sa_next = warp_active ? __ldg(p.a_scale + grow) : 0.f;
+        for (int kb = 0; kb < KB; ++kb) {
+          const float sw = __ldg(ws + kb);
+#pragma unroll
+          for (int gi = 0; gi < 2; ++gi) {
+            const int blk = 2 * kb + gi;    // 64-column block of the intermediate
+            const float sa = sa_next;
+            if (warp_active && blk + 1 < 2 * KB)
+              sa_next = __ldg(p.a_scale + static_cast<int64_t>(blk + 1) * p.npad + grow);
+            const float s = sa * sw;
+            const uint32_t buf = g & 1u;
+            if (!mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 5)) goto epi_done;
+            tc_fence_after();
+            if (warp_active) {
+              const uint32_t tb = t_lane + buf * kTileN + 128u * h;
+              float v[32];
+#pragma unroll
+              for (int ch = 0; ch < 4; ++ch) {
+                tmem_ld32(tb + 32u * ch, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; j += 2)
+                  ffma2(acc[ch * 32 + j], acc[ch * 32 + j + 1], v[j], v[j + 1], s);
+              }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            ++g;
+          }
+        }
+        // routing-weighted scatter-add into out[token] (kernel.py:236-250)
+        if (warp_active && row_valid) {
+          const float w = p.row_weight[grow];
+          const int tok = p.row_token[grow];
+          float* dst = p.out_f32 + static_cast<int64_t>(tok) * p.hidden + c.n * kTileN + 128 * h;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            red_add_v4(dst + 4 * j, acc[4 * j] * w, acc[4 * j + 1] * w, acc[4 * j + 2] * w,
+                       acc[4 * j + 3] * w);
+        }
+      }
+    }
+  epi_done:;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+int gemm_set_smem_attrs() {
+  const int smem = gemm_smem_bytes();
+  if (cudaFuncSetAttribute(moe_gemm_kernel<kGemm1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  if (cudaFuncSetAttribute(moe_gemm_kernel<kGemm2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  return MOE_OK;
+}
+
+int launch_gemm(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmParams& p,
+                int grid, cudaStream_t stream) {
+  const int smem = gemm_smem_bytes();
+  if (mode == kGemm1)
+    moe_gemm_kernel<kGemm1><<<grid, kGemmThreads, smem, stream>>>(tm_a, tm_b, p);
+  else
+    moe_gemm_kernel<kGemm2><<<grid, kGemmThreads, smem, stream>>>(tm_a, tm_b, p);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+}  // namespace moe

@@ -1,0 +1,98 @@
+// Kernel parameter blocks and launch constants shared by the host glue
+// (moe_api.cu) and the kernels (moe_route.cu, moe_gemm.cu).
+#pragma once
+
+#include "moe_common.cuh"
+
+namespace moe {
+
+constexpr int kMaxExperts = 256;       // E_global (and hence E_local) limit
+constexpr int kMaxTopK = 8;
+constexpr int kRouteThreads = 256;     // 8 warps, one token per warp at a time
+constexpr int kMaxTokensPerBlock = 256;
+constexpr int kTileM = 128;            // rows (assignments) per GEMM tile
+constexpr int kTileN = 256;            // output columns per GEMM tile
+constexpr int kBlockK = 128;           // K per pipeline stage = scale block
+constexpr int kInterScaleBlock = 64;   // requant granularity of the intermediate (kernel.py:643)
+constexpr int kStages = 4;             // smem pipeline depth
+constexpr int kGemmThreads = 384;      // warpgroups 0-1: epilogue; 2: TMA warp, MMA warp, 2 idle
+constexpr int kEpilogueRegs = 232;     // setmaxnreg split: 8*32*232 + 4*32*40 = 384*168
+constexpr int kControlRegs = 40;
+constexpr int kStageABytes = kTileM * kBlockK;     // 16 KB
+constexpr int kStageBBytes = kTileN * kBlockK;     // 32 KB
+constexpr int kStageBytes = kStageABytes + kStageBBytes;
+constexpr int kTmemCols = 512;         // two 256-column fp32 partial accumulators
+
+struct RouteParams {
+  const float* logits;
+  const void* bias;
+  int bias_dtype;
+  int T, E, n_group, topk_group, top_k;
+  int lanes_per_group, experts_per_lane;
+  int E_local, local_expert_offset;
+  float routed_scaling_factor;
+  int tokens_per_block;
+  int* topk_idx;
+  float* topk_weights;
+  int* block_base;   // [blocks, E_local]
+  int* counts;       // [E_local]
+  int* tile_start;   // [E_local + 1]
+  CtrlBlock* ctrl;
+};
+
+struct PermuteParams {
+  int T, H, top_k, E_local, local_expert_offset, tokens_per_block;
+  int64_t npad;
+  const int* topk_idx;
+  const float* topk_weights;
+  const int* block_base;
+  const int* tile_start;
+  const uint8_t* hidden;
+  const float* hs_scale;
+  int* row_token;
+  float* row_weight;
+  uint8_t* a_perm;
+  float* a_scale_perm;
+};
+
+// One persistent grouped GEMM launch.  Work units are (expert tile, N tile)
+// pairs, enumerated expert by expert with the N tile outer and the expert's
+// 128-row tiles inner, so consecutive units share a weight tile in L2.
+struct GemmParams {
+  const int* tile_start;   // [E_local + 1] prefix sum of 128-row tiles
+  const int* counts;       // [E_local] rows per expert
+  int E_local;
+  int num_k_blocks;        // K / 128
+  int n_tiles;             // N tiles of 256 output columns
+  int b_rows_per_expert;   // rows of one expert's weight matrix (2I or H)
+  int inter;               // I
+  int hidden;              // H
+  int64_t npad;            // row capacity of the permuted buffers
+  const float* a_scale;    // GEMM1: [H/128, npad]   GEMM2: [I/64, npad]
+  const float* b_scale;    // GEMM1: [E, 2I/128, H/128]   GEMM2: [E, H/128, I/128]
+  uint8_t* inter_out;      // GEMM1 output [npad, I] e4m3
+  float* inter_scale;      // GEMM1 output [I/64, npad]
+  const int* row_token;    // GEMM2: token of each permuted row
+  const float* row_weight; // GEMM2: routing weight of each permuted row
+  float* out_f32;          // GEMM2: [T, H] accumulator
+  CtrlBlock* ctrl;
+};
+
+__global__ void moe_route_kernel(RouteParams p);
+__global__ void moe_permute_kernel(PermuteParams p);
+__global__ void moe_finalize_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out,
+                                    int64_t n8);
+
+constexpr int kGemm1 = 0;   // gate/up GEMM, SwiGLU + 1x64 FP8 requant epilogue
+constexpr int kGemm2 = 1;   // down GEMM, routing-weighted scatter-add epilogue
+
+// Host-side launchers defined next to the kernel templates (moe_gemm.cu).
+int gemm_set_smem_attrs();
+int launch_gemm(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmParams& p,
+                int grid, cudaStream_t stream);
+
+constexpr int gemm_smem_bytes() {
+  return 1024 /*alignment slack*/ + kStages * kStageBytes + 4096 /*barriers + tables*/;
+}
+
+}  // namespace moe

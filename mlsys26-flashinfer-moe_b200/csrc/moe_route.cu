@@ -1,0 +1,274 @@
+// Routing and dispatch for the fused FP8 MoE forward (sm_100a).
+//
+//   moe_route_kernel    DeepSeek-V3 no-aux group-limited top-k router, one warp
+//                       per token, fused with the per-block expert histogram;
+//                       the last block to finish turns the histograms into
+//                       bucket offsets and the 128-row tile schedule.
+//                       Replaces moe_routing_kernel (reference kernel.py:428-542),
+//                       _count_kernel (252-285), the host sum/cumsum of
+//                       build_expert_dispatch (356-361) and build_tile_schedule
+//                       (384-407) -- without any device->host synchronisation.
+//   moe_permute_kernel  Places every (token, local expert) assignment at its
+//                       row of the expert-contiguous buffers, in token order
+//                       inside each expert, and packs the token's FP8 row and
+//                       scales there.  Replaces _scatter_kernel (288-324) and the
+//                       index_select packing (663-665).
+//   moe_finalize_kernel fp32 accumulator -> bf16 output (reference kernel.py:729).
+#include "moe_kernels.cuh"
+
+namespace moe {
+
+namespace {
+
+__device__ __forceinline__ float load_bias(const void* bias, int dtype, int i) {
+  if (dtype == MOE_BIAS_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[i]);
+  if (dtype == MOE_BIAS_F16) return __half2float(static_cast<const __half*>(bias)[i]);
+  return static_cast<const float*>(bias)[i];
+}
+
+// Sigmoid evaluated in double and rounded once to float, so that the result is
+// the correctly rounded float in all but astronomically rare cases and the
+// routing decisions are reproducible on any host.
+__device__ __forceinline__ float sigmoid_f32(float x) {
+  return static_cast<float>(1.0 / (1.0 + exp(-static_cast<double>(x))));
+}
+
+// One token on one warp.  Lane l holds experts [l*EPL, (l+1)*EPL); a group of
+// G experts spans LPG = G/EPL consecutive lanes.
+template <int EPL>
+__device__ __forceinline__ void route_one_token(const RouteParams& p, int t, int lane,
+                                                const float (&bias)[EPL], int* hist_s) {
+  const unsigned full = 0xffffffffu;
+  const int e0 = lane * EPL;
+  const bool active = e0 < p.E;
+  float s[EPL], sb[EPL];
+  const float* row = p.logits + static_cast<int64_t>(t) * p.E;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const float x = active ? __ldg(row + e0 + j) : 0.f;
+    s[j] = sigmoid_f32(x);
+    sb[j] = active ? s[j] + bias[j] : -INFINITY;
+  }
+  // --- group score: sum of the two largest sb in the group (kernel.py:479-488)
+  float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    if (sb[j] > m1) {
+      m2 = m1;
+      m1 = sb[j];
+    } else if (sb[j] > m2) {
+      m2 = sb[j];
+    }
+  }
+  for (int off = 1; off < p.lanes_per_group; off <<= 1) {
+    const float o1 = __shfl_xor_sync(full, m1, off);
+    const float o2 = __shfl_xor_sync(full, m2, off);
+    const float hi = fmaxf(m1, o1);
+    m2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+    m1 = hi;
+  }
+  const float gscore = m1 + m2;
+  // --- keep the topk_group best groups, ties to the lowest group (495-501)
+  const int my_group = lane / p.lanes_per_group;
+  int better = 0;
+  for (int g = 0; g < p.n_group; ++g) {
+    const float o = __shfl_sync(full, gscore, g * p.lanes_per_group);
+    better += (o > gscore) || (o == gscore && g < my_group);
+  }
+  const bool keep = active && better < p.topk_group;
+  float cand[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) cand[j] = keep ? sb[j] : -INFINITY;
+  // --- top_k experts by sb, ties to the lowest expert id (522-534)
+  int my_idx = 0;
+  float my_s = 0.f;
+  for (int k = 0; k < p.top_k; ++k) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      if (cand[j] > bv) {
+        bv = cand[j];
+        bi = e0 + j;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(full, bv, off);
+      const int oi = __shfl_xor_sync(full, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    float sv = 0.f;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      if (e0 + j == bi) {
+        sv = s[j];
+        cand[j] = -INFINITY;
+      }
+    }
+    sv = __shfl_sync(full, sv, min(bi / EPL, 31));
+    if (lane == k) {
+      my_idx = bi;
+      my_s = sv;
+    }
+  }
+  // --- renormalise by the unbiased scores (537-538)
+  float acc = (lane < p.top_k) ? my_s : 0.f;
+  float total;
+  if ((p.top_k & (p.top_k - 1)) == 0) {
+    for (int off = 1; off < p.top_k; off <<= 1) acc = acc + __shfl_down_sync(full, acc, off);
+    total = __shfl_sync(full, acc, 0);
+  } else {
+    total = __shfl_sync(full, my_s, 0);
+    for (int k = 1; k < p.top_k; ++k) total = total + __shfl_sync(full, my_s, k);
+  }
+  total = total + 1e-20f;
+  if (lane < p.top_k) {
+    const float w = __fdiv_rn(my_s, total) * p.routed_scaling_factor;
+    p.topk_idx[static_cast<int64_t>(t) * p.top_k + lane] = my_idx;
+    p.topk_weights[static_cast<int64_t>(t) * p.top_k + lane] = w;
+    const int le = my_idx - p.local_expert_offset;
+    if (le >= 0 && le < p.E_local) atomicAdd(&hist_s[le], 1);
+  }
+}
+
+template <int EPL>
+__device__ __forceinline__ void route_block_tokens(const RouteParams& p, int* hist_s) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float bias[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane * EPL + j;
+    bias[j] = e < p.E ? load_bias(p.bias, p.bias_dtype, e) : 0.f;
+  }
+  const int t0 = blockIdx.x * p.tokens_per_block;
+  const int t1 = min(p.T, t0 + p.tokens_per_block);
+  for (int t = t0 + warp; t < t1; t += kRouteThreads / 32) route_one_token<EPL>(p, t, lane, bias, hist_s);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p) {
+  __shared__ int hist_s[kMaxExperts];
+  __shared__ int warp_sum[kRouteThreads / 32];
+  __shared__ int is_last;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < p.E_local; i += kRouteThreads) hist_s[i] = 0;
+  __syncthreads();
+  switch (p.experts_per_lane) {
+    case 1: route_block_tokens<1>(p, hist_s); break;
+    case 2: route_block_tokens<2>(p, hist_s); break;
+    case 4: route_block_tokens<4>(p, hist_s); break;
+    default: route_block_tokens<8>(p, hist_s); break;
+  }
+  __syncthreads();
+  for (int i = tid; i < p.E_local; i += kRouteThreads)
+    p.block_base[static_cast<int64_t>(blockIdx.x) * p.E_local + i] = hist_s[i];
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = (atomicAdd(&p.ctrl->done, 1u) == static_cast<unsigned>(gridDim.x - 1));
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // Last block: per-expert exclusive scan over blocks -> bucket base of every
+  // block (token order is block order), per-expert counts, then the prefix sum
+  // of 128-row tiles that places every expert's segment in the permuted
+  // buffers.
+  int count = 0;
+  if (tid < p.E_local) {
+    for (int b = 0; b < static_cast<int>(gridDim.x); ++b) {
+      int* slot = p.block_base + static_cast<int64_t>(b) * p.E_local + tid;
+      const int v = __ldcg(slot);
+      *slot = count;
+      count += v;
+    }
+    p.counts[tid] = count;
+  }
+  const int tiles = tid < p.E_local ? (count + kTileM - 1) / kTileM : 0;
+  // block-wide exclusive scan of `tiles`
+  const int lane = tid & 31, warp = tid >> 5;
+  int incl = tiles;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (lane == 31) warp_sum[warp] = incl;
+  __syncthreads();
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += warp_sum[w];
+  incl += before;
+  if (tid < p.E_local) p.tile_start[tid] = incl - tiles;
+  if (tid == kRouteThreads - 1) p.tile_start[p.E_local] = incl;
+  if (tid == 0) p.ctrl->done = 0u;
+}
+
+__global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParams p) {
+  __shared__ int cursor[kMaxExperts];
+  __shared__ int rows_s[kMaxTokensPerBlock * kMaxTopK];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.x;
+  const int t0 = b * p.tokens_per_block;
+  const int t1 = min(p.T, t0 + p.tokens_per_block);
+  for (int i = tid; i < p.E_local; i += kRouteThreads)
+    cursor[i] = kTileM * p.tile_start[i] + p.block_base[static_cast<int64_t>(b) * p.E_local + i];
+  __syncthreads();
+  // Row of every assignment, tokens in order (a token's experts are distinct,
+  // so the lanes of one token never touch the same cursor).
+  if (warp == 0) {
+    for (int t = t0; t < t1; ++t) {
+      if (lane < p.top_k) {
+        const int le = p.topk_idx[static_cast<int64_t>(t) * p.top_k + lane] - p.local_expert_offset;
+        int row = -1;
+        if (le >= 0 && le < p.E_local) row = cursor[le]++;
+        rows_s[(t - t0) * p.top_k + lane] = row;
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  const int n_assign = (t1 - t0) * p.top_k;
+  const int hb = p.H / kBlockK;
+  for (int j = tid; j < n_assign; j += kRouteThreads) {
+    const int row = rows_s[j];
+    if (row < 0) continue;
+    const int t = t0 + j / p.top_k;
+    p.row_token[row] = t;
+    p.row_weight[row] = p.topk_weights[static_cast<int64_t>(t) * p.top_k + j % p.top_k];
+    for (int kb = 0; kb < hb; ++kb)
+      p.a_scale_perm[static_cast<int64_t>(kb) * p.npad + row] =
+          __ldg(p.hs_scale + static_cast<int64_t>(kb) * p.T + t);
+  }
+  // FP8 rows: one warp per assignment, 16-byte vectors.
+  const int vec = p.H / 16;
+  for (int j = warp; j < n_assign; j += kRouteThreads / 32) {
+    const int row = rows_s[j];
+    if (row < 0) continue;
+    const int t = t0 + j / p.top_k;
+    const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(t) * p.H);
+    uint4* dst = reinterpret_cast<uint4*>(p.a_perm + static_cast<int64_t>(row) * p.H);
+    for (int c = lane; c < vec; c += 32) dst[c] = __ldg(src + c);
+  }
+}
+
+__global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restrict__ in,
+                                                           __nv_bfloat16* __restrict__ out,
+                                                           int64_t n8) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += stride) {
+    const float4 a = __ldcs(reinterpret_cast<const float4*>(in) + 2 * i);
+    const float4 b = __ldcs(reinterpret_cast<const float4*>(in) + 2 * i + 1);
+    __nv_bfloat162 r[4];
+    r[0] = __floats2bfloat162_rn(a.x, a.y);
+    r[1] = __floats2bfloat162_rn(a.z, a.w);
+    r[2] = __floats2bfloat162_rn(b.x, b.y);
+    r[3] = __floats2bfloat162_rn(b.z, b.w);
+    reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<uint4*>(r);
+  }
+}
+
+}  // namespace moe
