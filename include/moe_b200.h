@@ -116,6 +116,15 @@ int moe_fp8_workspace_layout(const MoeFwdArgs* a, MoeWorkspaceLayout* out);
  * tokens routed elsewhere get zeros, as in the reference. */
 int moe_fp8_forward(const MoeFwdArgs* a, void* stream);
 
+/* moe_fp8_forward that also records CUDA events (cudaEvent_t handles, already
+ * created) on `stream` at the stage boundaries, for per-kernel timing:
+ *   events[0] start, [1] after routing (+ accumulator zeroing), [2] after the
+ *   permute/pack, [3] after GEMM1, [4] after GEMM2, [5] after the bf16 cast.
+ * n_events must be 6.  No counterpart in the reference (profiling aid). */
+#define MOE_PROFILE_EVENTS 6
+int moe_fp8_forward_profiled(const MoeFwdArgs* a, void* stream, void* const* events,
+                             int n_events);
+
 /* Routing only: writes topk_idx / topk_weights (and the dispatch counters) in
  * the workspace.  Replaces moe_routing_kernel (kernel.py:428-542) plus the
  * counting pass of build_expert_dispatch (kernel.py:252-285, 327-361). */

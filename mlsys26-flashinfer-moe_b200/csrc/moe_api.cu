@@ -236,16 +236,24 @@ int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
-int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
+int record(void* const* ev, int i, cudaStream_t s) {
+  if (!ev) return MOE_OK;
+  return cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
+                   void* const* ev = nullptr) {
   DeviceInfo* dev = nullptr;
   int st = device_info(&dev);
   if (st) return st;
+  if ((st = record(ev, 0, s))) return st;
   const MoeWorkspaceLayout& w = L.w;
   const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local;
   float* out_f32 = ws_ptr<float>(a, w.out_f32);
   if (cudaMemsetAsync(out_f32, 0, sizeof(float) * T * H, s) != cudaSuccess) return MOE_ERR_CUDA;
   st = launch_route(a, L, s);
   if (st) return st;
+  if ((st = record(ev, 1, s))) return st;
 
   PermuteParams pp{};
   pp.T = static_cast<int>(T);
@@ -267,6 +275,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
   pp.a_scale_perm = ws_ptr<float>(a, w.a_scale_perm);
   moe_permute_kernel<<<L.blocks, kRouteThreads, 0, s>>>(pp);
   if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+  if ((st = record(ev, 2, s))) return st;
 
   CUtensorMap tm_a1, tm_b1, tm_a2, tm_b2;
   if ((st = byte_tile_map(pp.a_perm, H, w.npad, &tm_a1))) return st;
@@ -290,6 +299,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
   g1.inter_scale = ws_ptr<float>(a, w.inter_scale);
   g1.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
   if ((st = launch_gemm(kGemm1, tm_a1, tm_b1, g1, dev->sms, s))) return st;
+  if ((st = record(ev, 3, s))) return st;
 
   GemmParams g2 = g1;
   g2.num_k_blocks = static_cast<int>(I / kBlockK);
@@ -303,12 +313,14 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
   g2.row_weight = pp.row_weight;
   g2.out_f32 = out_f32;
   if ((st = launch_gemm(kGemm2, tm_a2, tm_b2, g2, dev->sms, s))) return st;
+  if ((st = record(ev, 4, s))) return st;
 
   const int64_t n8 = T * H / 8;
   int blocks = static_cast<int>((n8 + 255) / 256);
   if (blocks > dev->sms * 8) blocks = dev->sms * 8;
   moe_finalize_kernel<<<blocks, 256, 0, s>>>(out_f32, static_cast<__nv_bfloat16*>(a->output), n8);
-  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+  return record(ev, 5, s);
 }
 
 }  // namespace
@@ -340,6 +352,16 @@ int moe_fp8_forward(const MoeFwdArgs* a, void* stream) {
   if (st) return st;
   if (a->T == 0) return MOE_OK;
   return launch_forward(a, L, static_cast<cudaStream_t>(stream));
+}
+
+int moe_fp8_forward_profiled(const MoeFwdArgs* a, void* stream, void* const* events,
+                             int n_events) {
+  if (!events || n_events != MOE_PROFILE_EVENTS) return MOE_ERR_INVALID_ARG;
+  Layout L;
+  int st = check_args(a, &L);
+  if (st) return st;
+  if (a->T == 0) return MOE_OK;
+  return launch_forward(a, L, static_cast<cudaStream_t>(stream), events);
 }
 
 int moe_fp8_route(const MoeFwdArgs* a, void* stream) {

@@ -22,6 +22,8 @@ MOE_ERR_CUDA = -5
 MOE_ERR_TIMEOUT = -6
 MOE_ERR_DEVICE = -7
 
+MOE_PROFILE_EVENTS = 6
+
 MOE_BIAS_F32 = 0
 MOE_BIAS_BF16 = 1
 MOE_BIAS_F16 = 2
@@ -83,6 +85,8 @@ SYMBOLS = {
     "moe_fp8_workspace_layout": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs),
                                                 ctypes.POINTER(MoeWorkspaceLayout)]),
     "moe_fp8_forward": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p]),
+    "moe_fp8_forward_profiled": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p,
+                                                ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]),
     "moe_fp8_route": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p]),
     "moe_fp8_device_error": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p,
                                             ctypes.POINTER(ctypes.c_int32),
