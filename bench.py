@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--no-extras", action="store_true",
                     help="skip decode / contest / e2e / cpu-baseline extras")
     ap.add_argument("--cpu-sample-tokens", type=int, default=16)
+    ap.add_argument("--e-local", type=int, default=256,
+                    help="local experts (0..e_local-1 of 256); < 256 gives the small "
+                         "same-density case used for ncu captures")
     return ap.parse_args()
 
 
@@ -292,7 +295,7 @@ def run_ours(a):
     torch.cuda.set_device(0)
     peaks, peak_kind = load_peaks()
     t = a.tokens or 8192
-    shape = workloads.dsv3_shape(t)
+    shape = workloads.dsv3_shape(t, e_local=a.e_local)
     runner = Runner(torch, shape, seed=0)
     clocks = ClockSampler(torch.cuda.current_device())
     # timed region: K forwards with per-stage events
@@ -312,10 +315,11 @@ def run_ours(a):
     stages = {n: statistics.mean(row[j].elapsed_time(row[j + 1]) for row in evs)
               for j, n in enumerate(names)}
     active = runner.active_experts()
-    flops = t * shape.top_k * workloads.flops_per_assignment(shape)
+    n_assign = int(runner.api.workspace_views(runner.args, runner.ws)["counts"].sum().item())
+    flops = n_assign * workloads.flops_per_assignment(shape)
     value = t / (ms * 1e-3)
     fp8_peak = fp8_cublas_peak_tflops(torch)
-    g1_flops = t * shape.top_k * 4 * shape.hidden * shape.inter
+    g1_flops = n_assign * 4 * shape.hidden * shape.inter
     g1_ms = stages["gemm1"]
     g1_bytes = active * 2 * shape.inter * shape.hidden
     roofline = {
@@ -334,9 +338,10 @@ def run_ours(a):
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp8-e4m3 x e4m3 -> fp32 (bf16 out)", "data": "synthetic (seeded, random-init weights)",
-        "config": {"workload": f"DeepSeek-V3 MoE layer, T={t}, 256 experts on 1 GPU (config 2)",
+        "config": {"workload": f"DeepSeek-V3 MoE layer, T={t}, {shape.e_local} of 256 experts "
+                               f"on 1 GPU" + (" (config 2)" if shape.e_local == 256 else ""),
                    "model": "DeepSeek-V3 MoE layer", "global_batch": t, "seq_len": 1,
-                   "hidden": shape.hidden, "intermediate": shape.inter, "experts": 256,
+                   "hidden": shape.hidden, "intermediate": shape.inter, "experts": shape.e_local,
                    "top_k": 8, "parallelism": "single GPU",
                    "l2": "weights 11.3 GB > L2 (no flush needed)"},
         "tflops": round(flops / (ms * 1e-3) / 1e12, 1),

@@ -48,6 +48,7 @@ extern "C" {
 #define MOE_ERR_CUDA (-5)            /* a CUDA runtime / driver call failed */
 #define MOE_ERR_TIMEOUT (-6)         /* a device-side bounded wait expired */
 #define MOE_ERR_DEVICE (-7)          /* device is not sm_100 */
+#define MOE_ERR_TOO_LARGE (-8)       /* beyond the fixed scratch of moe_fp8_route_noalloc */
 
 /* routing_bias element type */
 #define MOE_BIAS_F32 0
@@ -133,6 +134,33 @@ int moe_fp8_route(const MoeFwdArgs* a, void* stream);
 /* Device-side error word of the last forward on this workspace (0 = none).
  * Reads the control block with a blocking copy on `stream`. */
 int moe_fp8_device_error(const MoeFwdArgs* a, void* stream, int32_t* code, int32_t* info);
+
+/* Routing for callers that cannot allocate device memory.  No counterpart in
+ * the reference.
+ *
+ * Some hosts must not allocate while this layer runs: an inference engine's
+ * plugin callback where allocation is forbidden, a serving loop whose device
+ * memory is owned by another pool, or a foreign-language caller with no device
+ * allocator.  This entry point needs no workspace.  The caller passes the
+ * router inputs (logits [T, E_global] fp32, bias [E_global]) and the outputs:
+ * topk_idx [T, top_k] int32 and topk_weights [T, top_k] fp32 (as moe_fp8_route
+ * writes them) and expert_counts [E_local] int32 (assignments per local
+ * expert, the reference's token_counts, kernel.py:357).
+ *
+ * Scratch lives in a fixed device array inside the library (263,428 bytes) that
+ * every GPU which loads the library keeps until the process exits.  Limits:
+ * T <= 65536, E_global <= 256; larger sizes return MOE_ERR_TOO_LARGE.  The
+ * first call on each device looks up that array's device address (with the
+ * device current); make this first call before any stream capture.  All calls
+ * share the one array, so calls that overlap on the GPU (different streams,
+ * or different host threads on the same device) race: order them on a
+ * single stream. */
+int moe_fp8_route_noalloc(const float* routing_logits, const void* routing_bias,
+                          int32_t bias_dtype, int64_t T, int64_t E_global, int64_t n_group,
+                          int64_t topk_group, int64_t top_k, int64_t E_local,
+                          int64_t local_expert_offset, float routed_scaling_factor,
+                          int32_t* topk_idx, float* topk_weights, int32_t* expert_counts,
+                          void* stream);
 
 /* Human-readable name of a status code. */
 const char* moe_fp8_status_string(int code);

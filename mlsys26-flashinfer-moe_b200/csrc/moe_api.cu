@@ -402,6 +402,7 @@ const char* moe_fp8_status_string(int code) {
     case MOE_ERR_CUDA: return "CUDA call failed";
     case MOE_ERR_TIMEOUT: return "device-side wait timed out";
     case MOE_ERR_DEVICE: return "device is not sm_100 (B200)";
+    case MOE_ERR_TOO_LARGE: return "size exceeds the fixed scratch of moe_fp8_route_noalloc";
     default: return "unknown status";
   }
 }
@@ -416,3 +417,116 @@ int moe_fp8_num_sms(int device, int32_t* out) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Routing without a workspace.
+//
+// Some callers cannot allocate device memory at the point where they route
+// tokens: an inference engine that runs this layer from a plugin callback in
+// which allocation is forbidden, a serving loop whose device memory is owned in
+// full by another pool, or a host in another language that has no device
+// allocator to hand.  moe_fp8_route_noalloc serves them: it takes only the
+// router inputs and the caller's output arrays and keeps its scratch (the
+// per-block expert histograms, the tile prefix sum and the arrival counter of
+// the last-block scan) in the fixed device array below.  That array is part of
+// the library image, so every GPU that loads the library holds it
+// (kNoAllocScratchBytes = 263,428 bytes) until the process exits.
+// ---------------------------------------------------------------------------
+
+namespace moe {
+namespace {
+
+constexpr int kNoAllocMaxBlocks = 256;                 // route blocks for T <= 65536
+constexpr int64_t kNoAllocMaxTokens = 65536;
+constexpr size_t kNoAllocHistOffset = sizeof(CtrlBlock);
+constexpr size_t kNoAllocTileOffset =
+    kNoAllocHistOffset + sizeof(int) * kNoAllocMaxBlocks * kMaxExperts;
+constexpr size_t kNoAllocScratchBytes = kNoAllocTileOffset + sizeof(int) * (kMaxExperts + 1);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device.  Host code must not pass the
+// symbol itself to a kernel: on the host it names a host-side stand-in.
+unsigned char* g_noalloc_ptr[64];
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(unsigned char** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MOE_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return MOE_ERR_CUDA;
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return MOE_OK;
+}
+
+}  // namespace
+}  // namespace moe
+
+extern "C" int moe_fp8_route_noalloc(const float* routing_logits, const void* routing_bias,
+                                     int32_t bias_dtype, int64_t T, int64_t E_global,
+                                     int64_t n_group, int64_t topk_group, int64_t top_k,
+                                     int64_t E_local, int64_t local_expert_offset,
+                                     float routed_scaling_factor, int32_t* topk_idx,
+                                     float* topk_weights, int32_t* expert_counts,
+                                     void* stream) {
+  using namespace moe;
+  MoeFwdArgs a{};
+  a.T = T;
+  a.H = 256;                      // the router does not read H or I; any valid value
+  a.I = 128;
+  a.E_global = E_global;
+  a.E_local = E_local;
+  a.local_expert_offset = local_expert_offset;
+  a.n_group = n_group;
+  a.topk_group = topk_group;
+  a.top_k = top_k;
+  a.routed_scaling_factor = routed_scaling_factor;
+  a.bias_dtype = bias_dtype;
+  int st = validate_shape(&a);
+  if (st) return st;
+  if (T > kNoAllocMaxTokens) return MOE_ERR_TOO_LARGE;
+  if (T == 0) return MOE_OK;
+  if (!routing_logits || !routing_bias || !topk_idx || !topk_weights || !expert_counts)
+    return MOE_ERR_INVALID_ARG;
+  const Layout L = make_layout(&a);
+  if (L.blocks > kNoAllocMaxBlocks) return MOE_ERR_TOO_LARGE;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev))) return st;
+  unsigned char* scratch = nullptr;
+  if ((st = noalloc_scratch(&scratch))) return st;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  RouteParams rp{};
+  rp.logits = routing_logits;
+  rp.bias = routing_bias;
+  rp.bias_dtype = bias_dtype;
+  rp.T = static_cast<int>(T);
+  rp.E = static_cast<int>(E_global);
+  rp.n_group = static_cast<int>(n_group);
+  rp.topk_group = static_cast<int>(topk_group);
+  rp.top_k = static_cast<int>(top_k);
+  const int epl = rp.E <= 32 ? 1 : rp.E / 32;
+  rp.experts_per_lane = epl;
+  rp.lanes_per_group = (rp.E / rp.n_group) / epl;
+  rp.E_local = static_cast<int>(E_local);
+  rp.local_expert_offset = static_cast<int>(local_expert_offset);
+  rp.routed_scaling_factor = routed_scaling_factor;
+  rp.tokens_per_block = L.tokens_per_block;
+  rp.topk_idx = topk_idx;
+  rp.topk_weights = topk_weights;
+  rp.counts = expert_counts;
+  rp.ctrl = reinterpret_cast<CtrlBlock*>(scratch);
+  rp.block_base = reinterpret_cast<int*>(scratch + kNoAllocHistOffset);
+  rp.tile_start = reinterpret_cast<int*>(scratch + kNoAllocTileOffset);
+  // The array keeps the previous call's contents: the arrival counter of the
+  // last-block scan must start at zero.  Histograms and the tile prefix are
+  // fully rewritten by every call.
+  if (cudaMemsetAsync(scratch, 0, sizeof(CtrlBlock), s) != cudaSuccess) return MOE_ERR_CUDA;
+  moe_route_kernel<<<L.blocks, kRouteThreads, 0, s>>>(rp);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}

@@ -21,6 +21,7 @@ MOE_ERR_WORKSPACE = -4
 MOE_ERR_CUDA = -5
 MOE_ERR_TIMEOUT = -6
 MOE_ERR_DEVICE = -7
+MOE_ERR_TOO_LARGE = -8
 
 MOE_PROFILE_EVENTS = 6
 
@@ -91,6 +92,11 @@ SYMBOLS = {
     "moe_fp8_device_error": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p,
                                             ctypes.POINTER(ctypes.c_int32),
                                             ctypes.POINTER(ctypes.c_int32)]),
+    "moe_fp8_route_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_int64, ctypes.c_float, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "moe_fp8_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "moe_fp8_num_sms": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int32)]),
 }
