@@ -217,16 +217,6 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // numerics
 // ---------------------------------------------------------------------------
 
-// acc[0..1] += p[0..1] * s with the packed two-lane fp32 FMA of sm_100.
-__device__ __forceinline__ void ffma2(float& a0, float& a1, float p0, float p1, float s) {
-  uint64_t acc, pp, ss;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(acc) : "f"(a0), "f"(a1));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(pp) : "f"(p0), "f"(p1));
-  asm("mov.b64 %0, {%1, %1};" : "=l"(ss) : "f"(s));
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(pp), "l"(ss));
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc));
-}
-
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
                "f"(c), "f"(d)

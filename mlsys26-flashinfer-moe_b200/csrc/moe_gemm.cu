@@ -13,7 +13,8 @@
 //                         intermediate) K elements, which the tensor core
 //                         cannot apply, so every partial accumulator covers
 //                         exactly one scale block and is folded into fp32
-//                         registers as acc += partial * (sa[row] * sw[block]).
+//                         registers as acc += partial * (sa[row] * sw[block]),
+//                         reading 64 TMEM columns per wait.
 //                         Warp w reads TMEM lanes 32*(w%4).. and column half
 //                         w/4, so each thread owns one row and 128 columns.
 //
@@ -221,29 +222,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float* ws = p.b_scale + static_cast<int64_t>(c.e) * (2 * ib_rows) * KB;
         const float* ws_x1 = ws + static_cast<int64_t>(c.n) * KB;
         const float* ws_x2 = ws + static_cast<int64_t>(ib_rows + c.n) * KB;
-        float sa_next = warp_active ? __ldg(p.a_scale + grow) : 0.f;
+        // Scales of K block kb+1 are loaded while block kb is promoted.
+        float sa_n = warp_active ? __ldg(p.a_scale + grow) : 0.f;
+        float w1_n = __ldg(ws_x1), w2_n = __ldg(ws_x2);
         for (int kb = 0; kb < KB; ++kb) {
-          const float sa = sa_next;
-          if (warp_active && kb + 1 < KB)
-            sa_next = __ldg(p.a_scale + static_cast<int64_t>(kb + 1) * p.npad + grow);
-          const float s1 = sa * __ldg(ws_x1 + kb);
-          const float s2 = sa * __ldg(ws_x2 + kb);
+          const float s1 = sa_n * w1_n;
+          const float s2 = sa_n * w2_n;
+          if (kb + 1 < KB) {
+            if (warp_active)
+              sa_n = __ldg(p.a_scale + static_cast<int64_t>(kb + 1) * p.npad + grow);
+            w1_n = __ldg(ws_x1 + kb + 1);
+            w2_n = __ldg(ws_x2 + kb + 1);
+          }
           const uint32_t buf = g & 1u;
           if (!mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 4)) goto epi_done;
           tc_fence_after();
           if (warp_active) {
             const uint32_t tb = t_lane + buf * kTileN;
-            float v[32];
+            float v[64];
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-              // chunks 0,1: X1 columns 64h..64h+63; chunks 2,3: X2 columns 128+64h..
-              const uint32_t col = (ch < 2 ? 0u : 128u) + 64u * h + 32u * (ch & 1);
+            for (int half = 0; half < 2; ++half) {
+              // half 0: X1 columns 64h..64h+63; half 1: X2 columns 128+64h..
+              const uint32_t col = 128u * half + 64u * h;
               tmem_ld32(tb + col, v);
+              tmem_ld32(tb + col + 32, v + 32);
               tmem_ld_wait();
-              const float s = ch < 2 ? s1 : s2;
+              const float s = half == 0 ? s1 : s2;
 #pragma unroll
-              for (int j = 0; j < 32; j += 2)
-                ffma2(acc[ch * 32 + j], acc[ch * 32 + j + 1], v[j], v[j + 1], s);
+              for (int j = 0; j < 64; ++j) acc[half * 64 + j] = fmaf(v[j], s, acc[half * 64 + j]);
             }
           }
           tc_fence_before();
@@ -251,60 +257,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (lane == 0) mbar_arrive(&tempty[buf]);
           ++g;
         }
-        // SwiGLU + 1x64 requant (kernel.py:128-151)
+        // SwiGLU + 1x64 requant (kernel.py:128-151).  The MMA is stalled while
+        // this runs, so it uses one reciprocal per element for the sigmoid and
+        // one IEEE reciprocal of the scale per row instead of 128 divisions.
         if (warp_active) {
           float amax = 0.f;
 #pragma unroll
           for (int j = 0; j < 64; ++j) {
             const float x1 = acc[j], x2 = acc[64 + j];
-            const float cval = (x2 / (1.0f + expf(-x2))) * x1;
+            const float cval = (x2 * __frcp_rn(1.0f + __expf(-x2))) * x1;
             acc[j] = cval;
             amax = fmaxf(amax, fabsf(cval));
           }
           const float sc = fmaxf(amax / 448.0f, 1e-12f);
+          const float inv = 1.0f / sc;
           if (row_valid) {
-            uint32_t packed[16];
+            uint4* dst = reinterpret_cast<uint4*>(p.inter_out + grow * p.inter +
+                                                  c.n * (kTileN / 2) + 64 * h);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const uint32_t lo = pack_e4m3x2(acc[4 * j] / sc, acc[4 * j + 1] / sc);
-              const uint32_t hi = pack_e4m3x2(acc[4 * j + 2] / sc, acc[4 * j + 3] / sc);
-              packed[j] = lo | (hi << 16);
+            for (int q16 = 0; q16 < 4; ++q16) {
+              uint32_t w4[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float* a4 = acc + 16 * q16 + 4 * j;
+                w4[j] = pack_e4m3x2(a4[0] * inv, a4[1] * inv) |
+                        (pack_e4m3x2(a4[2] * inv, a4[3] * inv) << 16);
+              }
+              dst[q16] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
-            uint4* dst = reinterpret_cast<uint4*>(p.inter_out + grow * p.inter + c.n * (kTileN / 2) +
-                                                  64 * h);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                                  packed[4 * j + 3]);
             p.inter_scale[static_cast<int64_t>(2 * c.n + h) * p.npad + grow] = sc;
           }
         }
       } else {
         // W2 scale [E, H/128, I/128]: row block 2n + h of this thread's columns.
         const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * kb_rows + 2 * c.n + h) * KB;
-        float sa_next = warp_active ? __ldg(p.a_scale + grow) : 0.f;
+        float sa_n = warp_active ? __ldg(p.a_scale + grow) : 0.f;
+        float sw_n = __ldg(ws);
         for (int kb = 0; kb < KB; ++kb) {
-          const float sw = __ldg(ws + kb);
+          const float sw = sw_n;
+          if (kb + 1 < KB) sw_n = __ldg(ws + kb + 1);
 #pragma unroll
           for (int gi = 0; gi < 2; ++gi) {
             const int blk = 2 * kb + gi;    // 64-column block of the intermediate
-            const float sa = sa_next;
+            const float s = sa_n * sw;
             if (warp_active && blk + 1 < 2 * KB)
-              sa_next = __ldg(p.a_scale + static_cast<int64_t>(blk + 1) * p.npad + grow);
-            const float s = sa * sw;
+              sa_n = __ldg(p.a_scale + static_cast<int64_t>(blk + 1) * p.npad + grow);
             const uint32_t buf = g & 1u;
             if (!mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 5)) goto epi_done;
             tc_fence_after();
             if (warp_active) {
               const uint32_t tb = t_lane + buf * kTileN + 128u * h;
-              float v[32];
+              float v[64];
 #pragma unroll
-              for (int ch = 0; ch < 4; ++ch) {
-                tmem_ld32(tb + 32u * ch, v);
+              for (int half = 0; half < 2; ++half) {
+                tmem_ld32(tb + 64u * half, v);
+                tmem_ld32(tb + 64u * half + 32, v + 32);
                 tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 32; j += 2)
-                  ffma2(acc[ch * 32 + j], acc[ch * 32 + j + 1], v[j], v[j + 1], s);
+                for (int j = 0; j < 64; ++j) acc[half * 64 + j] = fmaf(v[j], s, acc[half * 64 + j]);
               }
             }
             tc_fence_before();
