@@ -87,13 +87,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait until the phase with the given parity of `bar` has completed.  Gives up
 // when `*abort` is raised by another warp or after kWaitLimitNs, in which case
 // it raises `*abort`, records MOE_ERR_TIMEOUT with `where` and returns false.
+// kBackoffNs > 0 sleeps between polls: used by the single-thread producer and
+// MMA roles so that their polling does not take issue slots from the promotion
+// warps sharing their sub-partition.
+template <unsigned kBackoffNs = 0>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           CtrlBlock* ctrl, int where) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
+    if (kBackoffNs) __nanosleep(kBackoffNs);
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if ((it & (kBackoffNs ? 15u : 255u)) == 0) {
       if (*abort) return false;
       if (globaltimer() - t0 > kWaitLimitNs) {
         *abort = 1;

@@ -5,16 +5,20 @@
 //   Warpgroup 2 (warps 8-11) gives registers to warpgroups 0-1 with setmaxnreg.
 //   warp 8  (one thread)  TMA producer: A tile 128x128 and B tile 256x128 (two
 //                         128-row boxes) per 128-deep K block, 4-stage ring.
-//   warp 9  (one thread)  MMA issuer: tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 ->
-//                         fp32), M=128 N=256 K=32, into one of two 256-column
-//                         TMEM partial accumulators.
+//   warps 9, 10 (one thread each) MMA issuers, one per TMEM partial buffer:
+//                         tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> fp32),
+//                         M=128 N=256 K=32, into one of two 256-column TMEM
+//                         partial accumulators.
 //   warps 0-7             Block-scale promotion and epilogue.  FP8 operands
 //                         carry one fp32 scale per 128 (A, W) or 64 (the
 //                         intermediate) K elements, which the tensor core
 //                         cannot apply, so every partial accumulator covers
 //                         exactly one scale block and is folded into fp32
 //                         registers as acc += partial * (sa[row] * sw[block]),
-//                         reading 64 TMEM columns per wait.
+//                         reading 64 TMEM columns per wait.  Only two partials
+//                         fit in TMEM, so the time a buffer is held bounds the
+//                         tensor core: a warp releases it right after its last
+//                         tcgen05.ld and does the remaining FMAs afterwards.
 //                         Warp w reads TMEM lanes 32*(w%4).. and column half
 //                         w/4, so each thread owns one row and 128 columns.
 //
@@ -66,6 +70,13 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Release a TMEM partial buffer once this warp's tcgen05.ld of it completed.
+__device__ __forceinline__ void release_buffer(uint64_t* tempty, int lane) {
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(tempty);
+}
+
 }  // namespace
 
 template <int kMode>
@@ -95,13 +106,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], kMode == kGemm1 ? 1 : 2);   // one commit per scale group
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, kMmaIssuers);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -134,7 +145,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                            (kMode == kGemm1 ? c.n * (kTileN / 2) : c.n * kTileN);
         const int b_row1 = kMode == kGemm1 ? b_row0 + p.inter : b_row0 + kTileN / 2;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 1)) goto producer_done;
+          if (!mbar_wait<kCtrlBackoffNs>(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 1)) goto producer_done;
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
           uint8_t* a_dst = sA + stage * kStageABytes;
           uint8_t* b_dst = sB + stage * kStageBBytes;
@@ -155,37 +166,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (issued & (1u << s)) drain_wait(&full[s], (issued_phase >> s) & 1u);
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 9 || warp == 10) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp 9 issues every scale group that writes TMEM buffer 0, warp 10 every
+    // group that writes buffer 1.  Each issuer waits only on its own buffer's
+    // "released" barrier and visits the stages in K order, so no barrier it
+    // waits on is ever more than one phase ahead (the parity waits need that),
+    // and the cost of issuing is split over two sub-partitions.
     if (lane == 0) {
       constexpr int kGroups = kMode == kGemm1 ? 1 : 2;   // scale blocks per K block
       constexpr int kMmaPerGroup = (kBlockK / 32) / kGroups;
+      const uint32_t me = static_cast<uint32_t>(warp - 9);   // = the buffer it fills
       const uint32_t idesc = umma_idesc_e4m3_f32(kTileM, kTileN);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t g = 0;
       for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.ctrl, 2)) goto mma_done;
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * kStageABytes);
-          const uint32_t b_base = smem_u32(sB + stage * kStageBBytes);
+          bool have_stage = false;
 #pragma unroll
-          for (int gi = 0; gi < kGroups; ++gi) {
-            const uint32_t buf = g & 1u;
-            if (!mbar_wait(&tempty[buf], ((g >> 1) & 1u) ^ 1u, abort_flag, p.ctrl, 3))
+          for (int gi = 0; gi < kGroups; ++gi, ++g) {
+            if ((g & 1u) != me) continue;
+            if (!have_stage) {
+              if (!mbar_wait<kCtrlBackoffNs>(&full[stage], phase, abort_flag, p.ctrl, 2)) goto mma_done;
+              have_stage = true;
+            }
+            if (!mbar_wait<kCtrlBackoffNs>(&tempty[me], ((g >> 1) & 1u) ^ 1u, abort_flag, p.ctrl, 3))
               goto mma_done;
             tc_fence_after();
+            const uint32_t a_base = smem_u32(sA + stage * kStageABytes);
+            const uint32_t b_base = smem_u32(sB + stage * kStageBBytes);
 #pragma unroll
             for (int kk = 0; kk < kMmaPerGroup; ++kk) {
               const uint32_t koff = static_cast<uint32_t>((gi * kMmaPerGroup + kk) * 32);
-              umma_f8(tmem_base + buf * kTileN, umma_desc_sw128(a_base + koff),
+              umma_f8(tmem_base + me * kTileN, umma_desc_sw128(a_base + koff),
                       umma_desc_sw128(b_base + koff), idesc, kk > 0 ? 1u : 0u);
             }
-            umma_commit(&tfull[buf]);
-            ++g;
+            umma_commit(&tfull[me]);
+            umma_commit(&empty[stage]);
           }
-          umma_commit(&empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -193,8 +212,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     mma_done:
-      // Every commit above arrives in order; once this one lands, all MMAs and
-      // their barrier arrivals are done and TMEM / smem can be released.
+      // Commits of one issuer arrive in order; once both issuers' drain
+      // commits have landed, every MMA and barrier arrival is done and TMEM /
+      // shared memory can be released.
       umma_commit(drain);
       drain_wait(drain, 0);
     }
@@ -240,21 +260,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (warp_active) {
             const uint32_t tb = t_lane + buf * kTileN;
             float v[64];
+            // X1 columns 64h..64h+63, then X2 columns 128+64h..; the buffer is
+            // released as soon as the last columns are in registers, before
+            // their FMAs (the hold time bounds the tensor core, see above).
+            tmem_ld32(tb + 64u * h, v);
+            tmem_ld32(tb + 64u * h + 32, v + 32);
+            tmem_ld_wait();
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              // half 0: X1 columns 64h..64h+63; half 1: X2 columns 128+64h..
-              const uint32_t col = 128u * half + 64u * h;
-              tmem_ld32(tb + col, v);
-              tmem_ld32(tb + col + 32, v + 32);
-              tmem_ld_wait();
-              const float s = half == 0 ? s1 : s2;
+            for (int i = 0; i < 64; ++i) acc[i] = fmaf(v[i], s1, acc[i]);
+            tmem_ld32(tb + 128u + 64u * h, v);
+            tmem_ld32(tb + 128u + 64u * h + 32, v + 32);
+            tmem_ld_wait();
+            release_buffer(&tempty[buf], lane);
 #pragma unroll
-              for (int j = 0; j < 64; ++j) acc[half * 64 + j] = fmaf(v[j], s, acc[half * 64 + j]);
-            }
+            for (int i = 0; i < 64; ++i) acc[64 + i] = fmaf(v[i], s2, acc[64 + i]);
+          } else {
+            release_buffer(&tempty[buf], lane);
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
           ++g;
         }
         // SwiGLU + 1x64 requant (kernel.py:128-151).  The MMA is stalled while
@@ -308,18 +330,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (warp_active) {
               const uint32_t tb = t_lane + buf * kTileN + 128u * h;
               float v[64];
+              tmem_ld32(tb, v);
+              tmem_ld32(tb + 32, v + 32);
+              tmem_ld_wait();
 #pragma unroll
-              for (int half = 0; half < 2; ++half) {
-                tmem_ld32(tb + 64u * half, v);
-                tmem_ld32(tb + 64u * half + 32, v + 32);
-                tmem_ld_wait();
+              for (int i = 0; i < 64; ++i) acc[i] = fmaf(v[i], s, acc[i]);
+              tmem_ld32(tb + 64, v);
+              tmem_ld32(tb + 96, v + 32);
+              tmem_ld_wait();
+              release_buffer(&tempty[buf], lane);
 #pragma unroll
-                for (int j = 0; j < 64; ++j) acc[half * 64 + j] = fmaf(v[j], s, acc[half * 64 + j]);
-              }
+              for (int i = 0; i < 64; ++i) acc[64 + i] = fmaf(v[i], s, acc[64 + i]);
+            } else {
+              release_buffer(&tempty[buf], lane);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);
             ++g;
           }
         }

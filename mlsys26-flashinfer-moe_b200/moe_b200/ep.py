@@ -1,0 +1,150 @@
+"""Expert parallelism for the fused FP8 MoE layer: one process per GPU.
+
+The reference already expresses an expert shard in its API
+(``local_expert_offset`` + a contiguous weight slice, kernel.py:572, 271-272)
+but leaves the exchange of tokens to the caller.  This module provides it:
+rank ``r`` of ``W`` owns experts ``[r*E/W, (r+1)*E/W)`` and its own tokens, and
+one forward is
+
+1. route the rank's tokens (``moe_fp8_route``) to find, per token, the ranks
+   that own at least one of its experts;
+2. exchange per-destination row counts (all-to-all of ``W`` ints, the only
+   host synchronisation: NCCL needs split sizes on the host);
+3. dispatch each token's FP8 row, its 1x128 scales and its router logits once
+   per destination rank (deduplicated), all-to-all-v over NCCL;
+4. run the fused layer (``moe_fp8_forward``) on the received rows with the
+   local expert slice; re-routing the received logits on the destination gives
+   exactly the source's expert choice (routing is a pure function of logits and
+   bias), and the kernel keeps only local experts;
+5. send the bf16 partial outputs back (all-to-all-v) and add them per token in
+   fixed rank order in fp32.
+
+Steps 1 and 4 are pluggable (``route_fn``, ``expert_fn``) so that the exchange
+logic runs on CPU ``gloo`` ranks in tests with the oracle as the expert
+compute; the product path uses the CUDA kernels and NCCL.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib, api
+
+
+def expert_range(rank: int, world: int, e_global: int):
+    assert e_global % world == 0, "experts must split evenly over ranks"
+    per = e_global // world
+    return rank * per, per
+
+
+def cuda_route(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+               gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+               routed_scaling_factor, n_group, topk_group, top_k):
+    """topk_idx [T, top_k] int32 of the rank's own tokens via ``moe_fp8_route``."""
+    t, h = hidden_states.shape
+    dummy = torch.empty(t, h, dtype=torch.bfloat16, device=hidden_states.device)
+    args, keep, _ = api.build_args(routing_logits, routing_bias, hidden_states,
+                                   hidden_states_scale, gemm1_weights, gemm1_weights_scale,
+                                   gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                                   routed_scaling_factor, dummy, n_group, topk_group, top_k)
+    lay = api.workspace_layout(args)
+    stream = torch.cuda.current_stream()
+    ws = api.get_workspace(lay.total_bytes, hidden_states.device, stream)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    code = _lib.load().moe_fp8_route(ctypes.byref(args), ctypes.c_void_p(stream.cuda_stream))
+    if code:
+        raise _lib.MoeError(code, "moe_fp8_route")
+    return api.workspace_views(args, ws)["topk_idx"].clone()
+
+
+def cuda_expert(logits, bias, x, xs_t, w1, w1s, w2, w2s, offset, rsf, out, n_group, topk_group,
+                top_k):
+    api.run(logits, bias, x, xs_t, w1, w1s, w2, w2s, offset, rsf, out, n_group=n_group,
+            topk_group=topk_group, top_k=top_k)
+
+
+def _a2a(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group):
+    """all_to_all_single on byte views (NCCL has no fp8 type)."""
+    o = out.view(torch.uint8) if out.dtype in (torch.float8_e4m3fn,) else out
+    i = inp.view(torch.uint8) if inp.dtype in (torch.float8_e4m3fn,) else inp
+    dist.all_to_all_single(o, i, out_splits, in_splits, group=group)
+
+
+@torch.no_grad()
+def ep_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+               gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, routed_scaling_factor,
+               output, *, group=None, n_group=8, topk_group=4, top_k=8,
+               route_fn: Optional[Callable] = None, expert_fn: Optional[Callable] = None,
+               timings: Optional[dict] = None):
+    """Expert-parallel forward of this rank's tokens; writes bf16 ``output``.
+
+    ``gemm*_weights`` are this rank's contiguous expert slice (``E/W`` experts
+    starting at ``rank*E/W``); ``routing_bias`` is the layer's bias and must be
+    the same on every rank (destinations re-route the rows they receive).  All
+    ranks must call together (collectives).
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    t, h = hidden_states.shape
+    e_global = routing_logits.shape[1]
+    lo, per = expert_range(rank, world, e_global)
+    assert gemm1_weights.shape[0] == per, "weights must be this rank's expert slice"
+    dev = hidden_states.device
+    route_fn = route_fn or cuda_route
+    expert_fn = expert_fn or cuda_expert
+
+    # 1. destinations of every token
+    idx = route_fn(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                   gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, lo,
+                   routed_scaling_factor, n_group, topk_group, top_k)
+    dest = (idx.long() // per)                                   # [T, top_k]
+    mask = torch.zeros(t, world, dtype=torch.bool, device=dev)
+    if t:
+        mask.scatter_(1, dest, True)
+    pairs = mask.t().nonzero()                                   # (rank, token), rank-major
+    send_tok = pairs[:, 1].contiguous()
+    send_counts = mask.sum(0).to(torch.int64)
+
+    # 2. counts exchange (host sync for the NCCL split sizes)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    sc = send_counts.tolist()
+    rc = recv_counts.tolist()
+    n_recv = int(sum(rc))
+
+    # 3. dispatch FP8 rows, scales (row-major) and logits, once per destination
+    send_x = hidden_states.index_select(0, send_tok)
+    send_s = hidden_states_scale.index_select(1, send_tok).t().contiguous()
+    send_l = routing_logits.index_select(0, send_tok)
+    recv_x = torch.empty(n_recv, h, dtype=hidden_states.dtype, device=dev)
+    recv_s = torch.empty(n_recv, h // 128, dtype=torch.float32, device=dev)
+    recv_l = torch.empty(n_recv, e_global, dtype=torch.float32, device=dev)
+    _a2a(recv_x, send_x, rc, sc, group)
+    _a2a(recv_s, send_s, rc, sc, group)
+    _a2a(recv_l, send_l, rc, sc, group)
+
+    # 4. local experts on the received rows
+    part = torch.empty(n_recv, h, dtype=torch.bfloat16, device=dev)
+    if n_recv:
+        expert_fn(recv_l, routing_bias, recv_x, recv_s.t().contiguous(), gemm1_weights,
+                  gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, lo,
+                  routed_scaling_factor, part, n_group, topk_group, top_k)
+
+    # 5. combine: partial rows back to their source, fixed-order fp32 sum
+    back = torch.empty(len(send_tok), h, dtype=torch.bfloat16, device=dev)
+    _a2a(back, part, sc, rc, group)
+    acc = torch.zeros(t, h, dtype=torch.float32, device=dev)
+    start = 0
+    for d in range(world):
+        n = sc[d]
+        if n:
+            acc.index_add_(0, send_tok[start:start + n], back[start:start + n].float())
+        start += n
+    output.copy_(acc.to(torch.bfloat16))
+    if timings is not None:
+        timings["rows_sent"] = len(send_tok)
+        timings["rows_received"] = n_recv
+    return output
