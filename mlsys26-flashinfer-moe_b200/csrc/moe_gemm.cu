@@ -70,6 +70,13 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Byte offset of 16-byte chunk c (0..3) of row r (0..31) in a warp's 32 x 64 B
+// staging tile.  The XOR swizzle keeps both access patterns free of bank
+// conflicts: row-wise writes (a quarter-warp writes one chunk of 8 rows) and
+// column-wise reads (a quarter-warp reads the 4 chunks of 2 rows) each touch 8
+// distinct 16-byte bank groups.
+__device__ __forceinline__ int xpose_off(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
+
 // Release a TMEM partial buffer once this warp's tcgen05.ld of it completed.
 __device__ __forceinline__ void release_buffer(uint64_t* tempty, int lane) {
   tc_fence_before();
@@ -88,7 +95,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kStageABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kStageBBytes);
+  uint8_t* xpose = sB + kStages * kStageBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(xpose + kXposeBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -293,22 +301,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           const float sc = fmaxf(amax / 448.0f, 1e-12f);
           const float inv = 1.0f / sc;
-          if (row_valid) {
-            uint4* dst = reinterpret_cast<uint4*>(p.inter_out + grow * p.inter +
-                                                  c.n * (kTileN / 2) + 64 * h);
+          // Each lane's 64 FP8 codes go through the warp's staging tile; the
+          // stores then write 64 contiguous bytes of 8 rows per instruction
+          // instead of 16 bytes of 32 rows.
+          uint8_t* stg = xpose + warp * kXposeBytesPerWarp;
 #pragma unroll
-            for (int q16 = 0; q16 < 4; ++q16) {
-              uint32_t w4[4];
+          for (int q16 = 0; q16 < 4; ++q16) {
+            uint32_t w4[4];
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float* a4 = acc + 16 * q16 + 4 * j;
-                w4[j] = pack_e4m3x2(a4[0] * inv, a4[1] * inv) |
-                        (pack_e4m3x2(a4[2] * inv, a4[3] * inv) << 16);
-              }
-              dst[q16] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            for (int j = 0; j < 4; ++j) {
+              const float* a4 = acc + 16 * q16 + 4 * j;
+              w4[j] = pack_e4m3x2(a4[0] * inv, a4[1] * inv) |
+                      (pack_e4m3x2(a4[2] * inv, a4[3] * inv) << 16);
             }
-            p.inter_scale[static_cast<int64_t>(2 * c.n + h) * p.npad + grow] = sc;
+            *reinterpret_cast<uint4*>(stg + xpose_off(lane, q16)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
+          __syncwarp();
+          uint8_t* dst = p.inter_out + static_cast<int64_t>(c.row0 + q * 32) * p.inter +
+                         c.n * (kTileN / 2) + 64 * h + 16 * (lane & 3);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rr = 8 * i + (lane >> 2);
+            if (q * 32 + rr < c.nrows)
+              *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(rr) * p.inter) =
+                  *reinterpret_cast<const uint4*>(stg + xpose_off(rr, lane & 3));
+          }
+          __syncwarp();
+          if (row_valid) p.inter_scale[static_cast<int64_t>(2 * c.n + h) * p.npad + grow] = sc;
         }
       } else {
         // W2 scale [E, H/128, I/128]: row block 2n + h of this thread's columns.
@@ -347,15 +366,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ++g;
           }
         }
-        // routing-weighted scatter-add into out[token] (kernel.py:236-250)
-        if (warp_active && row_valid) {
-          const float w = p.row_weight[grow];
-          const int tok = p.row_token[grow];
-          float* dst = p.out_f32 + static_cast<int64_t>(tok) * p.hidden + c.n * kTileN + 128 * h;
+        // Routing-weighted scatter-add into out[token] (kernel.py:236-250).
+        // Every row goes to a different token, so a lane-per-row red.v4
+        // touches 32 rows x 16 B per instruction.  The weighted values go
+        // through the warp's staging tile 16 columns at a time instead, and
+        // each red.v4 instruction then adds 64 contiguous bytes to 8 rows.
+        if (warp_active) {
+          const float w = row_valid ? p.row_weight[grow] : 0.f;
+          const int tok = row_valid ? p.row_token[grow] : 0;
+          float* stg = reinterpret_cast<float*>(xpose + warp * kXposeBytesPerWarp);
+          float* dst_i[4];
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            red_add_v4(dst + 4 * j, acc[4 * j] * w, acc[4 * j + 1] * w, acc[4 * j + 2] * w,
-                       acc[4 * j + 3] * w);
+          for (int i = 0; i < 4; ++i) {
+            const int rr = 8 * i + (lane >> 2);
+            const int t_i = __shfl_sync(0xffffffffu, tok, rr);
+            dst_i[i] = q * 32 + rr < c.nrows
+                           ? p.out_f32 + static_cast<int64_t>(t_i) * p.hidden + c.n * kTileN +
+                                 128 * h + 4 * (lane & 3)
+                           : nullptr;
+          }
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float* a4 = acc + 16 * ch + 4 * j;
+              *reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(stg) + xpose_off(lane, j)) =
+                  make_float4(a4[0] * w, a4[1] * w, a4[2] * w, a4[3] * w);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int rr = 8 * i + (lane >> 2);
+              const float4 v4 = *reinterpret_cast<const float4*>(
+                  reinterpret_cast<const uint8_t*>(stg) + xpose_off(rr, lane & 3));
+              if (dst_i[i]) red_add_v4(dst_i[i] + 16 * ch, v4.x, v4.y, v4.z, v4.w);
+            }
+            __syncwarp();
+          }
         }
       }
     }

@@ -23,6 +23,10 @@ constexpr int kMmaIssuers = 2;        // warps 9 and 10, one per TMEM buffer
 constexpr int kStageABytes = kTileM * kBlockK;     // 16 KB
 constexpr int kStageBBytes = kTileN * kBlockK;     // 32 KB
 constexpr int kStageBytes = kStageABytes + kStageBBytes;
+// Per promotion warp, a 32-row x 64-byte staging tile that transposes the
+// epilogue's row-per-lane results so that global writes go out row-contiguous.
+constexpr int kXposeBytesPerWarp = 32 * 64;
+constexpr int kXposeBytes = 8 * kXposeBytesPerWarp;
 constexpr int kTmemCols = 512;         // two 256-column fp32 partial accumulators
 
 struct RouteParams {
@@ -94,7 +98,8 @@ int launch_gemm(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, cons
                 int grid, cudaStream_t stream);
 
 constexpr int gemm_smem_bytes() {
-  return 1024 /*alignment slack*/ + kStages * kStageBytes + 4096 /*barriers + tables*/;
+  return 1024 /*alignment slack*/ + kStages * kStageBytes + kXposeBytes +
+         4096 /*barriers + tables*/;
 }
 
 }  // namespace moe
