@@ -72,14 +72,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// A thread whose try_wait finds the phase incomplete is suspended until the
+// phase completes or this many nanoseconds pass, whichever comes first: waiting
+// threads neither spin (which takes issue slots from the promotion warps on the
+// same sub-partition) nor sleep past the completion (which delays the hand-off).
+constexpr uint32_t kSuspendHintNs = 10000000u;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -87,24 +93,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait until the phase with the given parity of `bar` has completed.  Gives up
 // when `*abort` is raised by another warp or after kWaitLimitNs, in which case
 // it raises `*abort`, records MOE_ERR_TIMEOUT with `where` and returns false.
-// kBackoffNs > 0 sleeps between polls: used by the single-thread producer and
-// MMA roles so that their polling does not take issue slots from the promotion
-// warps sharing their sub-partition.
-template <unsigned kBackoffNs = 0>
+// Every unsuccessful try_wait has already suspended the thread for up to
+// kSuspendHintNs, so the abort flag and the clock are checked on each round.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           CtrlBlock* ctrl, int where) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  for (uint32_t it = 1;; ++it) {
-    if (kBackoffNs) __nanosleep(kBackoffNs);
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & (kBackoffNs ? 15u : 255u)) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        report_error(ctrl, MOE_ERR_TIMEOUT, where);
-        return false;
-      }
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      report_error(ctrl, MOE_ERR_TIMEOUT, where);
+      return false;
     }
   }
 }

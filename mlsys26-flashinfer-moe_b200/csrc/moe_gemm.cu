@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                            (kMode == kGemm1 ? c.n * (kTileN / 2) : c.n * kTileN);
         const int b_row1 = kMode == kGemm1 ? b_row0 + p.inter : b_row0 + kTileN / 2;
         for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait<kCtrlBackoffNs>(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 1)) goto producer_done;
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 1)) goto producer_done;
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
           uint8_t* a_dst = sA + stage * kStageABytes;
           uint8_t* b_dst = sB + stage * kStageBBytes;
@@ -196,10 +196,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int gi = 0; gi < kGroups; ++gi, ++g) {
             if ((g & 1u) != me) continue;
             if (!have_stage) {
-              if (!mbar_wait<kCtrlBackoffNs>(&full[stage], phase, abort_flag, p.ctrl, 2)) goto mma_done;
+              if (!mbar_wait(&full[stage], phase, abort_flag, p.ctrl, 2)) goto mma_done;
               have_stage = true;
             }
-            if (!mbar_wait<kCtrlBackoffNs>(&tempty[me], ((g >> 1) & 1u) ^ 1u, abort_flag, p.ctrl, 3))
+            if (!mbar_wait(&tempty[me], ((g >> 1) & 1u) ^ 1u, abort_flag, p.ctrl, 3))
               goto mma_done;
             tc_fence_after();
             const uint32_t a_base = smem_u32(sA + stage * kStageABytes);

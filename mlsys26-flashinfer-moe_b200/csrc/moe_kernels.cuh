@@ -18,7 +18,6 @@ constexpr int kStages = 4;             // smem pipeline depth
 constexpr int kGemmThreads = 384;      // warpgroups 0-1: epilogue; 2: TMA warp, MMA warp, 2 idle
 constexpr int kEpilogueRegs = 232;     // setmaxnreg split: 8*32*232 + 4*32*40 = 384*168
 constexpr int kControlRegs = 40;
-constexpr unsigned kCtrlBackoffNs = 64;   // poll interval of producer / MMA waits
 constexpr int kMmaIssuers = 2;        // warps 9 and 10, one per TMEM buffer
 constexpr int kStageABytes = kTileM * kBlockK;     // 16 KB
 constexpr int kStageBBytes = kTileN * kBlockK;     // 32 KB
