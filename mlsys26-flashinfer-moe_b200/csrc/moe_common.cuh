@@ -90,6 +90,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking check of a phase: issued early, its latency hides behind work
+// that does not depend on the answer.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity of `bar` has completed.  Gives up
 // when `*abort` is raised by another warp or after kWaitLimitNs, in which case
 // it raises `*abort`, records MOE_ERR_TIMEOUT with `where` and returns false.
@@ -189,6 +203,43 @@ __device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+
+// One scale group of MMAs, D = A0*B0^T + A1*B1^T (+ ...), issued from one asm
+// block with descriptors computed beforehand.  The issuing thread shares its
+// sub-partition with promotion warps that stream FMAs and win most issue
+// slots, so every instruction between "buffer free" and the last MMA costs
+// far more than its latency; this keeps that window to the MMAs themselves.
+template <int kCount>
+__device__ __forceinline__ void umma_f8_group(uint32_t d_tmem, const uint64_t* a, const uint64_t* b,
+                                              uint32_t idesc) {
+  static_assert(kCount == 2 || kCount == 4, "groups of 2 or 4 MMAs");
+  if constexpr (kCount == 2) {
+    asm volatile(
+        "{\n\t.reg .pred f, t;\n\t"
+        "setp.ne.b32 f, %5, %5;\n\t"
+        "setp.eq.b32 t, %5, %5;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %3, %5, f;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %4, %5, t;\n\t}" ::"r"(d_tmem),
+        "l"(a[0]), "l"(a[1]), "l"(b[0]), "l"(b[1]), "r"(idesc)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred f, t;\n\t"
+        "setp.ne.b32 f, %9, %9;\n\t"
+        "setp.eq.b32 t, %9, %9;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %5, %9, f;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %2, %6, %9, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %3, %7, %9, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %4, %8, %9, t;\n\t}" ::"r"(d_tmem),
+        "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]),
+        "r"(idesc)
+        : "memory");
+  }
+}
+
+// Forces values to be computed at this point of the program (before the
+// volatile asm that follows, e.g. a barrier wait).
+__device__ __forceinline__ void materialize(uint64_t v) { asm volatile("" ::"l"(v)); }
 
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread
 // has completed.

@@ -186,6 +186,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr int kMmaPerGroup = (kBlockK / 32) / kGroups;
       const uint32_t me = static_cast<uint32_t>(warp - 9);   // = the buffer it fills
       const uint32_t idesc = umma_idesc_e4m3_f32(kTileM, kTileN);
+      const uint32_t d_tmem = tmem_base + me * kTileN;
+      const uint64_t a_desc0 = umma_desc_sw128(smem_u32(sA));
+      const uint64_t b_desc0 = umma_desc_sw128(smem_u32(sB));
       int stage = 0;
       uint32_t phase = 0;
       uint32_t g = 0;
@@ -195,6 +198,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int gi = 0; gi < kGroups; ++gi, ++g) {
             if ((g & 1u) != me) continue;
+            // Descriptors of this group's K slices: the start-address field is
+            // the low bits, so slices and stages are plain offsets (>> 4).
+            uint64_t a_d[kMmaPerGroup], b_d[kMmaPerGroup];
+#pragma unroll
+            for (int kk = 0; kk < kMmaPerGroup; ++kk) {
+              const uint32_t koff = static_cast<uint32_t>((gi * kMmaPerGroup + kk) * 32);
+              a_d[kk] = a_desc0 + ((static_cast<uint32_t>(stage) * kStageABytes + koff) >> 4);
+              b_d[kk] = b_desc0 + ((static_cast<uint32_t>(stage) * kStageBBytes + koff) >> 4);
+              materialize(a_d[kk]);
+              materialize(b_d[kk]);
+            }
             if (!have_stage) {
               if (!mbar_wait(&full[stage], phase, abort_flag, p.ctrl, 2)) goto mma_done;
               have_stage = true;
@@ -202,14 +216,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (!mbar_wait(&tempty[me], ((g >> 1) & 1u) ^ 1u, abort_flag, p.ctrl, 3))
               goto mma_done;
             tc_fence_after();
-            const uint32_t a_base = smem_u32(sA + stage * kStageABytes);
-            const uint32_t b_base = smem_u32(sB + stage * kStageBBytes);
-#pragma unroll
-            for (int kk = 0; kk < kMmaPerGroup; ++kk) {
-              const uint32_t koff = static_cast<uint32_t>((gi * kMmaPerGroup + kk) * 32);
-              umma_f8(tmem_base + me * kTileN, umma_desc_sw128(a_base + koff),
-                      umma_desc_sw128(b_base + koff), idesc, kk > 0 ? 1u : 0u);
-            }
+            umma_f8_group<kMmaPerGroup>(d_tmem, a_d, b_d, idesc);
             umma_commit(&tfull[me]);
             umma_commit(&empty[stage]);
           }
@@ -238,6 +245,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t g = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
       const Unit c = decode_unit(u, tstart_s, counts_s, E, NT);
+      // Whether the next group's partial is already known to be complete:
+      // checked right after a buffer is released, so that the check's
+      // latency overlaps the FMAs that follow instead of stalling the warp.
+      bool next_ready = false;
       const bool warp_active = q * 32 < c.nrows;
       const bool row_valid = r < c.nrows;
       const int64_t grow = static_cast<int64_t>(c.row0) + r;
@@ -263,7 +274,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             w2_n = __ldg(ws_x2 + kb + 1);
           }
           const uint32_t buf = g & 1u;
-          if (!mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 4)) goto epi_done;
+          if (!next_ready && !mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 4))
+            goto epi_done;
           tc_fence_after();
           if (warp_active) {
             const uint32_t tb = t_lane + buf * kTileN;
@@ -280,10 +292,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tmem_ld32(tb + 128u + 64u * h + 32, v + 32);
             tmem_ld_wait();
             release_buffer(&tempty[buf], lane);
+            next_ready = mbar_test_wait(&tfull[buf ^ 1u], ((g + 1) >> 1) & 1u);
 #pragma unroll
             for (int i = 0; i < 64; ++i) acc[64 + i] = fmaf(v[i], s2, acc[64 + i]);
           } else {
             release_buffer(&tempty[buf], lane);
+            next_ready = false;
           }
           ++g;
         }
@@ -344,7 +358,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (warp_active && blk + 1 < 2 * KB)
               sa_n = __ldg(p.a_scale + static_cast<int64_t>(blk + 1) * p.npad + grow);
             const uint32_t buf = g & 1u;
-            if (!mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 5)) goto epi_done;
+            if (!next_ready && !mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 5))
+              goto epi_done;
             tc_fence_after();
             if (warp_active) {
               const uint32_t tb = t_lane + buf * kTileN + 128u * h;
@@ -358,10 +373,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               tmem_ld32(tb + 96, v + 32);
               tmem_ld_wait();
               release_buffer(&tempty[buf], lane);
+              next_ready = mbar_test_wait(&tfull[buf ^ 1u], ((g + 1) >> 1) & 1u);
 #pragma unroll
               for (int i = 0; i < 64; ++i) acc[64 + i] = fmaf(v[i], s, acc[64 + i]);
             } else {
               release_buffer(&tempty[buf], lane);
+              next_ready = false;
             }
             ++g;
           }
