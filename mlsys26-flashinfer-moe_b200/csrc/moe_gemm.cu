@@ -346,17 +346,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else {
         // W2 scale [E, H/128, I/128]: row block 2n + h of this thread's columns.
         const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * kb_rows + 2 * c.n + h) * KB;
-        float sa_n = warp_active ? __ldg(p.a_scale + grow) : 0.f;
+        // Both intermediate scales of K block kb+1 and its weight scale are
+        // loaded at the top of K block kb, a full K block (two groups) ahead
+        // of their use.
+        const float* sa_p = p.a_scale + grow;
+        float sa0_n = warp_active ? __ldg(sa_p) : 0.f;
+        float sa1_n = warp_active ? __ldg(sa_p + p.npad) : 0.f;
         float sw_n = __ldg(ws);
         for (int kb = 0; kb < KB; ++kb) {
-          const float sw = sw_n;
-          if (kb + 1 < KB) sw_n = __ldg(ws + kb + 1);
+          const float sg0 = sa0_n * sw_n, sg1 = sa1_n * sw_n;
+          if (kb + 1 < KB) {
+            if (warp_active) {
+              sa0_n = __ldg(sa_p + static_cast<int64_t>(2 * kb + 2) * p.npad);
+              sa1_n = __ldg(sa_p + static_cast<int64_t>(2 * kb + 3) * p.npad);
+            }
+            sw_n = __ldg(ws + kb + 1);
+          }
 #pragma unroll
           for (int gi = 0; gi < 2; ++gi) {
-            const int blk = 2 * kb + gi;    // 64-column block of the intermediate
-            const float s = sa_n * sw;
-            if (warp_active && blk + 1 < 2 * KB)
-              sa_n = __ldg(p.a_scale + static_cast<int64_t>(blk + 1) * p.npad + grow);
+            const float s = gi == 0 ? sg0 : sg1;
             const uint32_t buf = g & 1u;
             if (!next_ready && !mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 5))
               goto epi_done;
