@@ -116,6 +116,7 @@ int device_info(DeviceInfo** out) {
   if (d.major != 10) return MOE_ERR_DEVICE;
   if (!d.attrs_set) {
     if (gemm_set_smem_attrs() != MOE_OK) return MOE_ERR_CUDA;
+    if (gemm_small_set_smem_attrs() != MOE_OK) return MOE_ERR_CUDA;
     d.attrs_set = true;
   }
   *out = &d;
@@ -141,8 +142,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 struct MapKey {
   const void* base;
   uint64_t cols, rows;
+  uint32_t box_rows;
   bool operator==(const MapKey& o) const {
-    return base == o.base && cols == o.cols && rows == o.rows;
+    return base == o.base && cols == o.cols && rows == o.rows && box_rows == o.box_rows;
   }
 };
 struct MapEntry {
@@ -154,8 +156,11 @@ constexpr int kMapCache = 64;
 MapEntry g_maps[kMapCache];
 int g_map_next = 0;
 
-int byte_tile_map(const void* base, uint64_t cols, uint64_t rows, CUtensorMap* out) {
-  const MapKey key{base, cols, rows};
+// Tensor map of a row-major byte matrix [rows, cols] read in boxes of 128
+// columns (one K block) x box_rows rows, 128-byte swizzled.
+int byte_tile_map(const void* base, uint64_t cols, uint64_t rows, CUtensorMap* out,
+                  uint32_t box_rows = kTileM) {
+  const MapKey key{base, cols, rows, box_rows};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     for (int i = 0; i < kMapCache; ++i)
@@ -169,7 +174,7 @@ int byte_tile_map(const void* base, uint64_t cols, uint64_t rows, CUtensorMap* o
   CUtensorMap m;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(kTileM)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -277,10 +282,15 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
   if ((st = record(ev, 2, s))) return st;
 
+  // Decode-shaped batches (few rows per expert on average) take the
+  // swapped-operand kernels; the choice only depends on the shape, never on
+  // the routing, and both paths are exact for any routing.
+  const bool small = a->T * a->top_k <= kSmallPathMaxAvgRows * a->E_global;
+  const uint32_t tok_box = small ? 16u : static_cast<uint32_t>(kTileM);
   CUtensorMap tm_a1, tm_b1, tm_a2, tm_b2;
-  if ((st = byte_tile_map(pp.a_perm, H, w.npad, &tm_a1))) return st;
+  if ((st = byte_tile_map(pp.a_perm, H, w.npad, &tm_a1, tok_box))) return st;
   if ((st = byte_tile_map(a->gemm1_weights, H, El * 2 * I, &tm_b1))) return st;
-  if ((st = byte_tile_map(ws_ptr<uint8_t>(a, w.inter), I, w.npad, &tm_a2))) return st;
+  if ((st = byte_tile_map(ws_ptr<uint8_t>(a, w.inter), I, w.npad, &tm_a2, tok_box))) return st;
   if ((st = byte_tile_map(a->gemm2_weights, I, El * H, &tm_b2))) return st;
 
   GemmParams g1{};
@@ -298,7 +308,11 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   g1.inter_out = ws_ptr<uint8_t>(a, w.inter);
   g1.inter_scale = ws_ptr<float>(a, w.inter_scale);
   g1.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
-  if ((st = launch_gemm(kGemm1, tm_a1, tm_b1, g1, dev->sms, s))) return st;
+  if (small) {
+    if ((st = launch_gemm_small(kGemm1, tm_b1, tm_a1, g1, dev->sms, s))) return st;
+  } else if ((st = launch_gemm(kGemm1, tm_a1, tm_b1, g1, dev->sms, s))) {
+    return st;
+  }
   if ((st = record(ev, 3, s))) return st;
 
   GemmParams g2 = g1;
@@ -312,7 +326,12 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   g2.row_token = pp.row_token;
   g2.row_weight = pp.row_weight;
   g2.out_f32 = out_f32;
-  if ((st = launch_gemm(kGemm2, tm_a2, tm_b2, g2, dev->sms, s))) return st;
+  if (small) {
+    g2.n_tiles = static_cast<int>(H / kTileM);
+    if ((st = launch_gemm_small(kGemm2, tm_b2, tm_a2, g2, dev->sms, s))) return st;
+  } else if ((st = launch_gemm(kGemm2, tm_a2, tm_b2, g2, dev->sms, s))) {
+    return st;
+  }
   if ((st = record(ev, 4, s))) return st;
 
   const int64_t n8 = T * H / 8;

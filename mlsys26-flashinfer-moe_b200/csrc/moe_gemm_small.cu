@@ -1,0 +1,468 @@
+// Grouped GEMMs for decode-shaped batches (a few rows per expert), with the
+// operands swapped: the expert's weight rows are the MMA's M=128 operand and
+// up to 16 of its permuted token rows the N=16 operand.
+//
+// With 128-row token tiles a decode step would spend a full promotion pass
+// (two 256-column TMEM round trips per thread) on every 128-deep K block for
+// one to eight real rows.  Here a TMEM accumulator group is 128 lanes x 16 (or
+// 2 x 16) columns, eight of them fit in the 256 allocated columns, so the
+// tensor core runs up to eight groups ahead of the promotion and the kernel
+// streams weights at the rate HBM delivers them.
+//
+// One CTA per SM walks work units (expert, 128 output features, 16 token rows):
+//   warps 0-3  promotion + epilogue; thread (warp q, lane l) owns output feature
+//              32q + l of the unit for all 16 token columns.
+//   warp 4     TMA producer: per 128-deep K block the weight box(es) 128 x 128
+//              and the 16 x 128 token box, into a ring of kStagesS stages.
+//   warp 5     MMA issuer: tcgen05.mma kind::f8f6f4, M=128 N=16 K=32.
+//
+// kGemm1 (reference moe_gemm1_kernel, kernel.py:7-151): per unit two MMA
+//   chains into the two 16-column halves of a 32-column group, X1 = rows
+//   n*128.. of W1[e] (multiplied) and X2 = rows I + n*128.. (SiLU input);
+//   epilogue C = silu(X2) * X1, amax over 64 features (two warps), scale =
+//   max(amax/448, 1e-12), C * (1/scale) -> e4m3, written to the intermediate.
+// kGemm2 (reference moe_gemm2_kernel, kernel.py:153-250): W2[e] rows n*128..,
+//   two 64-deep scale groups per K block (the intermediate's 1x64 scales),
+//   epilogue out[token] += weight * D with fp32 reductions, 128 contiguous
+//   floats per token and warp.
+#include "moe_kernels.cuh"
+
+namespace moe {
+
+namespace {
+
+constexpr int kSmallN = 16;                // token rows per unit (MMA N)
+constexpr int kSmallThreads = 192;
+constexpr int kSmallTmemCols = 256;
+constexpr int kSmallBufs = 8;              // TMEM groups of 32 columns
+constexpr int kSmallBufCols = 32;
+constexpr int kTokBytes = kSmallN * kBlockK;   // 2 KB token box per K block
+
+template <int kMode>
+struct SmallCfg {
+  static constexpr int kWBytes = kMode == kGemm1 ? 2 * kTileM * kBlockK : kTileM * kBlockK;
+  static constexpr int kStageBytes = kWBytes + kTokBytes;
+  static constexpr int kStages = kMode == kGemm1 ? 6 : 11;
+  static constexpr int kGroups = kMode == kGemm1 ? 1 : 2;   // scale groups per K block
+};
+
+template <int kMode>
+constexpr int small_smem_bytes() {
+  return 1024 + SmallCfg<kMode>::kStages * SmallCfg<kMode>::kStageBytes + 4096 +
+         (2 * kMaxExperts + 2) * 4;
+}
+
+struct SmallUnit {
+  int e, n, row0, nrows;
+};
+
+__device__ __forceinline__ SmallUnit decode_small(int u, const int* ustart, const int* counts,
+                                                  const int* tstart, int E, int NT) {
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (ustart[mid] <= u) lo = mid;
+    else hi = mid - 1;
+  }
+  SmallUnit c;
+  c.e = lo;
+  const int mt = (counts[lo] + kSmallN - 1) / kSmallN;
+  const int l = u - ustart[lo];
+  c.n = l / mt;
+  const int t = l - c.n * mt;
+  c.row0 = tstart[lo] * kTileM + t * kSmallN;
+  c.nrows = min(kSmallN, counts[lo] - t * kSmallN);
+  return c;
+}
+
+__device__ __forceinline__ void drain_wait_s(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) return;
+  }
+}
+
+// Barrier among the four promotion warps on an mbarrier (count 4, one arrival
+// per warp), so that a warp leaving after an abort cannot strand the others.
+__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, int lane,
+                                         volatile int* abort, CtrlBlock* ctrl) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, phase & 1u, abort, ctrl, 16);
+  ++phase;
+  return ok;
+}
+
+}  // namespace
+
+template <int kMode>
+__global__ void __launch_bounds__(kSmallThreads, 1)
+    moe_gemm_small_kernel(const __grid_constant__ CUtensorMap tm_w,
+                          const __grid_constant__ CUtensorMap tm_tok, GemmParams p) {
+  using Cfg = SmallCfg<kMode>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sW = smem;                                   // S x kWBytes (1024-aligned)
+  uint8_t* sT = smem + S * Cfg::kWBytes;                // S x 2 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(sT + S * kTokBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + kSmallBufs;
+  uint64_t* drain = tempty + kSmallBufs;
+  uint64_t* ebar = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red_s = reinterpret_cast<float*>(tmem_slot + 2);     // [4][16] amax exchange
+  int* ustart_s = reinterpret_cast<int*>(red_s + 4 * kSmallN);
+  int* counts_s = ustart_s + kMaxExperts + 1;
+  int* tstart_s = counts_s + kMaxExperts;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = p.E_local, NT = p.n_tiles, KB = p.num_k_blocks;
+
+  for (int i = threadIdx.x; i < E; i += kSmallThreads) {
+    counts_s[i] = p.counts[i];
+    tstart_s[i] = p.tile_start[i];
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // Unit prefix over experts: NT x ceil(count / 16) units each, warp scan
+    // of up to 8 experts per lane.
+    int local[kMaxExperts / 32];
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+      const int e = lane * (kMaxExperts / 32) + j;
+      const int v = e < E ? NT * ((counts_s[e] + kSmallN - 1) / kSmallN) : 0;
+      local[j] = sum;
+      sum += v;
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int base = incl - sum;
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+      const int e = lane * (kMaxExperts / 32) + j;
+      if (e <= E) ustart_s[e] = base + local[j];
+    }
+    if (lane == 31 && E == kMaxExperts) ustart_s[E] = incl;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < kSmallBufs; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
+    mbar_init(ebar, 4);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, kSmallTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_tok);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_units = ustart_s[E];
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_phase = 0;
+      for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+        const SmallUnit c = decode_small(u, ustart_s, counts_s, tstart_s, E, NT);
+        const int w_row0 = c.e * p.b_rows_per_expert + c.n * kTileM;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 11)) goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          uint8_t* w_dst = sW + stage * Cfg::kWBytes;
+          tma_load_2d(w_dst, &tm_w, &full[stage], kb * kBlockK, w_row0);
+          if constexpr (kMode == kGemm1)
+            tma_load_2d(w_dst + kTileM * kBlockK, &tm_w, &full[stage], kb * kBlockK,
+                        w_row0 + p.inter);
+          tma_load_2d(sT + stage * kTokBytes, &tm_tok, &full[stage], kb * kBlockK, c.row0);
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      if (*abort_flag) {
+        for (int s = 0; s < S; ++s)
+          if (issued & (1u << s)) drain_wait_s(&full[s], (issued_phase >> s) & 1u);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_e4m3_f32(kTileM, kSmallN);
+      const uint64_t w_desc0 = umma_desc_sw128(smem_u32(sW));
+      const uint64_t t_desc0 = umma_desc_sw128(smem_u32(sT));
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t g = 0;
+      for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.ctrl, 12)) goto mma_done;
+          tc_fence_after();
+          const uint64_t wd = w_desc0 + ((static_cast<uint32_t>(stage) * Cfg::kWBytes) >> 4);
+          const uint64_t td = t_desc0 + ((static_cast<uint32_t>(stage) * kTokBytes) >> 4);
+#pragma unroll
+          for (int gi = 0; gi < Cfg::kGroups; ++gi, ++g) {
+            const uint32_t buf = g % kSmallBufs;
+            if (!mbar_wait(&tempty[buf], ((g / kSmallBufs) & 1u) ^ 1u, abort_flag, p.ctrl, 13))
+              goto mma_done;
+            tc_fence_after();
+            const uint32_t d = tmem_base + buf * kSmallBufCols;
+            if constexpr (kMode == kGemm1) {
+              uint64_t a[4], b[4], a2[4];
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                a[kk] = wd + ((kk * 32) >> 4);
+                a2[kk] = wd + ((kTileM * kBlockK + kk * 32) >> 4);
+                b[kk] = td + ((kk * 32) >> 4);
+              }
+              umma_f8_group<4>(d, a, b, idesc);
+              umma_f8_group<4>(d + kSmallN, a2, b, idesc);
+            } else {
+              uint64_t a[2], b[2];
+#pragma unroll
+              for (int kk = 0; kk < 2; ++kk) {
+                a[kk] = wd + (((gi * 2 + kk) * 32) >> 4);
+                b[kk] = td + (((gi * 2 + kk) * 32) >> 4);
+              }
+              umma_f8_group<2>(d, a, b, idesc);
+            }
+            umma_commit(&tfull[buf]);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    mma_done:
+      umma_commit(drain);
+      drain_wait_s(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ promotion + epilogue
+    const int q = warp;                       // TMEM lane quarter = feature rows 32q..
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t g = 0;
+    uint32_t ephase = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+      const SmallUnit c = decode_small(u, ustart_s, counts_s, tstart_s, E, NT);
+      constexpr int kAcc = kMode == kGemm1 ? 2 * kSmallN : kSmallN;
+      float acc[kAcc];
+#pragma unroll
+      for (int i = 0; i < kAcc; ++i) acc[i] = 0.f;
+      const float* sa_p = p.a_scale + c.row0;      // + block * npad: 16 contiguous scales
+      if constexpr (kMode == kGemm1) {
+        // W1 scale [E, 2I/128, H/128]: X1 block n, X2 block I/128 + n.
+        const int ib = p.inter / kBlockK;
+        const float* ws_x1 = p.b_scale + (static_cast<int64_t>(c.e) * 2 * ib + c.n) * KB;
+        const float* ws_x2 = ws_x1 + static_cast<int64_t>(ib) * KB;
+        // Groups are consumed kBatch1 at a time: all their TMEM loads go out
+        // before one tcgen05.wait::ld, so a batch costs one TMEM round trip.
+        // The batch's scales are requested before its barrier waits.
+        constexpr int kBatch1 = 2;
+        for (int kb0 = 0; kb0 < KB; kb0 += kBatch1) {
+          float sa[kBatch1][kSmallN], w1[kBatch1], w2[kBatch1];
+          uint32_t bufs[kBatch1];
+#pragma unroll
+          for (int bi = 0; bi < kBatch1; ++bi) {
+            const int kb = kb0 + bi;
+            if (kb < KB) {
+              const float4* s4 = reinterpret_cast<const float4*>(sa_p + static_cast<int64_t>(kb) * p.npad);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 f = __ldg(s4 + j);
+                sa[bi][4 * j] = f.x; sa[bi][4 * j + 1] = f.y; sa[bi][4 * j + 2] = f.z; sa[bi][4 * j + 3] = f.w;
+              }
+              w1[bi] = __ldg(ws_x1 + kb);
+              w2[bi] = __ldg(ws_x2 + kb);
+            }
+          }
+#pragma unroll
+          for (int bi = 0; bi < kBatch1; ++bi) {
+            const uint32_t gg = g + bi;
+            bufs[bi] = gg % kSmallBufs;
+            if (kb0 + bi < KB &&
+                !mbar_wait(&tfull[bufs[bi]], (gg / kSmallBufs) & 1u, abort_flag, p.ctrl, 14))
+              goto epi_done;
+          }
+          tc_fence_after();
+          float v[kBatch1][32];
+#pragma unroll
+          for (int bi = 0; bi < kBatch1; ++bi)
+            if (kb0 + bi < KB) tmem_ld32(t_lane + bufs[bi] * kSmallBufCols, v[bi]);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+#pragma unroll
+          for (int bi = 0; bi < kBatch1; ++bi)
+            if (kb0 + bi < KB && lane == 0) mbar_arrive(&tempty[bufs[bi]]);
+#pragma unroll
+          for (int bi = 0; bi < kBatch1; ++bi) {
+            if (kb0 + bi < KB) {
+#pragma unroll
+              for (int j = 0; j < kSmallN; ++j) {
+                acc[j] = fmaf(v[bi][j], sa[bi][j] * w1[bi], acc[j]);
+                acc[kSmallN + j] = fmaf(v[bi][kSmallN + j], sa[bi][j] * w2[bi], acc[kSmallN + j]);
+              }
+              ++g;
+            }
+          }
+        }
+        // SwiGLU + 1x64 requant (kernel.py:128-151): amax over the 64 features
+        // of this thread's half (warps 0-1 or 2-3) for every token column.
+        float cv[kSmallN];
+#pragma unroll
+        for (int j = 0; j < kSmallN; ++j) {
+          const float x1 = acc[j], x2 = acc[kSmallN + j];
+          cv[j] = (x2 * __frcp_rn(1.0f + __expf(-x2))) * x1;
+          float m = fabsf(cv[j]);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0) red_s[q * kSmallN + j] = m;
+        }
+        if (!epi_sync(ebar, ephase, lane, abort_flag, p.ctrl)) goto epi_done;
+        const int qp = q ^ 1;
+        const int col = c.n * kTileM + q * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < kSmallN; ++j) {
+          if (j < c.nrows) {
+            const float amax = fmaxf(red_s[q * kSmallN + j], red_s[qp * kSmallN + j]);
+            const float sc = fmaxf(amax / 448.0f, 1e-12f);
+            const float inv = 1.0f / sc;
+            const int64_t row = static_cast<int64_t>(c.row0) + j;
+            p.inter_out[row * p.inter + col] = static_cast<uint8_t>(pack_e4m3x2(cv[j] * inv, 0.f) & 0xffu);
+            if (lane == 0 && (q & 1) == 0)
+              p.inter_scale[static_cast<int64_t>(2 * c.n + (q >> 1)) * p.npad + row] = sc;
+          }
+        }
+        // red_s is rewritten by the next unit
+        if (!epi_sync(ebar, ephase, lane, abort_flag, p.ctrl)) goto epi_done;
+      } else {
+        // W2 scale [E, H/128, I/128]; intermediate scales [I/64, npad].
+        const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * (p.hidden / kBlockK) + c.n) * KB;
+        // Scale groups (two per K block) are consumed kBatch2 at a time, as in
+        // GEMM1.
+        constexpr int kBatch2 = 4;
+        const int ngroups = 2 * KB;
+        for (int g0 = 0; g0 < ngroups; g0 += kBatch2) {
+          float sa[kBatch2][kSmallN], sw[kBatch2];
+          uint32_t bufs[kBatch2];
+#pragma unroll
+          for (int bi = 0; bi < kBatch2; ++bi) {
+            const int gi = g0 + bi;
+            if (gi < ngroups) {
+              const float4* s4 = reinterpret_cast<const float4*>(sa_p + static_cast<int64_t>(gi) * p.npad);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 f = __ldg(s4 + j);
+                sa[bi][4 * j] = f.x; sa[bi][4 * j + 1] = f.y; sa[bi][4 * j + 2] = f.z; sa[bi][4 * j + 3] = f.w;
+              }
+              sw[bi] = __ldg(ws + (gi >> 1));
+            }
+          }
+#pragma unroll
+          for (int bi = 0; bi < kBatch2; ++bi) {
+            const uint32_t gg = g + bi;
+            bufs[bi] = gg % kSmallBufs;
+            if (g0 + bi < ngroups &&
+                !mbar_wait(&tfull[bufs[bi]], (gg / kSmallBufs) & 1u, abort_flag, p.ctrl, 15))
+              goto epi_done;
+          }
+          tc_fence_after();
+          float v[kBatch2][kSmallN];
+#pragma unroll
+          for (int bi = 0; bi < kBatch2; ++bi)
+            if (g0 + bi < ngroups) tmem_ld16(t_lane + bufs[bi] * kSmallBufCols, v[bi]);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+#pragma unroll
+          for (int bi = 0; bi < kBatch2; ++bi)
+            if (g0 + bi < ngroups && lane == 0) mbar_arrive(&tempty[bufs[bi]]);
+#pragma unroll
+          for (int bi = 0; bi < kBatch2; ++bi) {
+            if (g0 + bi < ngroups) {
+#pragma unroll
+              for (int j = 0; j < kSmallN; ++j) acc[j] = fmaf(v[bi][j], sa[bi][j] * sw[bi], acc[j]);
+              ++g;
+            }
+          }
+        }
+        // out[token] += weight * D (kernel.py:236-250): per token, the warp's 32
+        // lanes add 32 consecutive floats.
+        const int col = c.n * kTileM + q * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < kSmallN; ++j) {
+          if (j < c.nrows) {
+            const int64_t row = static_cast<int64_t>(c.row0) + j;
+            const int tok = __ldg(p.row_token + row);
+            const float w = __ldg(p.row_weight + row);
+            atomicAdd(p.out_f32 + static_cast<int64_t>(tok) * p.hidden + col, acc[j] * w);
+          }
+        }
+      }
+    }
+  epi_done:;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kSmallTmemCols);
+  }
+}
+
+int gemm_small_set_smem_attrs() {
+  if (cudaFuncSetAttribute(moe_gemm_small_kernel<kGemm1>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           small_smem_bytes<kGemm1>()) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  if (cudaFuncSetAttribute(moe_gemm_small_kernel<kGemm2>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           small_smem_bytes<kGemm2>()) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  return MOE_OK;
+}
+
+int launch_gemm_small(int mode, const CUtensorMap& tm_w, const CUtensorMap& tm_tok,
+                      const GemmParams& p, int grid, cudaStream_t stream) {
+  if (mode == kGemm1)
+    moe_gemm_small_kernel<kGemm1><<<grid, kSmallThreads, small_smem_bytes<kGemm1>(), stream>>>(
+        tm_w, tm_tok, p);
+  else
+    moe_gemm_small_kernel<kGemm2><<<grid, kSmallThreads, small_smem_bytes<kGemm2>(), stream>>>(
+        tm_w, tm_tok, p);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+}  // namespace moe

@@ -96,6 +96,17 @@ int gemm_set_smem_attrs();
 int launch_gemm(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, const GemmParams& p,
                 int grid, cudaStream_t stream);
 
+// The forward takes the decode-shaped GEMMs when T * top_k <= this many rows
+// per routed expert on average.
+constexpr int64_t kSmallPathMaxAvgRows = 4;
+
+// Decode-shaped variant with swapped operands (moe_gemm_small.cu): weight rows
+// are the M=128 operand, 16 permuted token rows the N operand.  n_tiles counts
+// 128-feature tiles for both GEMMs.
+int gemm_small_set_smem_attrs();
+int launch_gemm_small(int mode, const CUtensorMap& tm_w, const CUtensorMap& tm_tok,
+                      const GemmParams& p, int grid, cudaStream_t stream);
+
 constexpr int gemm_smem_bytes() {
   return 1024 /*alignment slack*/ + kStages * kStageBytes + kXposeBytes +
          4096 /*barriers + tables*/;

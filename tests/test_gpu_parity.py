@@ -140,6 +140,21 @@ def test_prefill_routing_permutation_and_sampled_output(cuda_device, t, zipf):
     assert np.isfinite(bf16_np(out)).all()
 
 
+@pytest.mark.parametrize("t,e_local,zipf", [(100, 256, 1.2), (60, 256, 2.0)])
+def test_decode_path_skewed_routing(cuda_device, t, e_local, zipf):
+    """Decode-sized batches take the swapped-operand kernels (rows per expert on
+    average <= 4); skewed routing gives some experts several 16-row token tiles."""
+    inp, shape = dsv3_inputs(t, seed=21 + t, e_local=e_local, zipf=zipf)
+    out, views, _ = run_cuda(inp, shape)
+    _, _, counts, _, _ = check_routing_and_dispatch(views, inp, shape)
+    assert counts.max() > 16
+    toks = np.random.default_rng(t).choice(t, 10, replace=False)
+    ref = oracle_output(inp, shape, tokens=toks)
+    got = bf16_np(out)[toks]
+    assert mo.cosine(got, ref) >= COS
+    np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
+
+
 def test_zero_tokens_is_a_noop(cuda_device):
     inp, shape = dsv3_inputs(0, seed=1, e_local=32)
     out, _, _ = run_cuda(inp, shape)
