@@ -402,24 +402,48 @@ def e2e_run(torch, runner, a):
 
 
 def decode_sweep(torch, peaks):
-    from moe_b200 import workloads
+    """Decode latency (T=1..64, all 256 experts), L2 flushed before every step:
+    p50 of the eager forward (five launches, no per-stage events), p50 of the
+    same forward replayed as one CUDA graph (``moe_b200.LayerGraph``), and a
+    per-stage breakdown from a separate run with stage events."""
+    from moe_b200 import workloads, LayerGraph
     res = {}
     flush_buf = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
 
     def flush():
         flush_buf.zero_()
+
+    def p50_of(fn, n=30, warm=5):
+        for _ in range(warm):
+            fn()
+        per = []
+        for _ in range(n):
+            flush()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            per.append(s.elapsed_time(e))
+        return statistics.median(per)
     for t in (1, 8, 32, 64):
         shape = workloads.dsv3_shape(t)
         r = Runner(torch, shape, seed=1)
-        _, stages, per = time_steps(torch, r, 30, 5, profile=True, flush=flush)
+        _, stages, _ = time_steps(torch, r, 10, 3, profile=True, flush=flush)
+        eager = p50_of(lambda: r.forward())
+        out_g = torch.empty_like(r.out)
+        graph = LayerGraph(*workloads.run_args(r.inp), out_g)
+        graphed = p50_of(graph.replay)
         active = r.active_experts()
-        p50 = statistics.median(per)
         byts = algorithmic_bytes(shape, active, t)
-        res[str(t)] = {"p50_us": round(p50 * 1e3, 1), "active_experts": active,
-                       "hbm_roofline_us": round(byts / (peaks["hbm_gbs"] * 1e9) * 1e6, 1),
-                       "hbm_frac": round(byts / (peaks["hbm_gbs"] * 1e9) / (p50 * 1e-3), 3),
+        roof = byts / (peaks["hbm_gbs"] * 1e9)
+        res[str(t)] = {"p50_us": round(eager * 1e3, 1), "p50_us_graph": round(graphed * 1e3, 1),
+                       "active_experts": active,
+                       "hbm_roofline_us": round(roof * 1e6, 1),
+                       "hbm_frac": round(roof / (eager * 1e-3), 3),
+                       "hbm_frac_graph": round(roof / (graphed * 1e-3), 3),
                        "stage_us": {k: round(v * 1e3, 1) for k, v in stages.items()}}
-        del r
+        del graph, r
         torch.cuda.empty_cache()
     return res
 

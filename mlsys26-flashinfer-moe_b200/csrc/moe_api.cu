@@ -285,7 +285,8 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   // Decode-shaped batches (few rows per expert on average) take the
   // swapped-operand kernels; the choice only depends on the shape, never on
   // the routing, and both paths are exact for any routing.
-  const bool small = a->T * a->top_k <= kSmallPathMaxAvgRows * a->E_global;
+  const bool small = a->T * a->top_k <= kSmallPathMaxAvgRows * a->E_global &&
+                     H / kBlockK <= kSmallMaxScaleBlocks && I / 64 <= kSmallMaxScaleBlocks;
   const uint32_t tok_box = small ? 16u : static_cast<uint32_t>(kTileM);
   CUtensorMap tm_a1, tm_b1, tm_a2, tm_b2;
   if ((st = byte_tile_map(pp.a_perm, H, w.npad, &tm_a1, tok_box))) return st;

@@ -37,6 +37,12 @@ constexpr int kSmallTmemCols = 256;
 constexpr int kSmallBufs = 8;              // TMEM groups of 32 columns
 constexpr int kSmallBufCols = 32;
 constexpr int kTokBytes = kSmallN * kBlockK;   // 2 KB token box per K block
+// Scale blocks per unit staged in shared memory: activation / intermediate
+// scale blocks (H/128 for GEMM1, I/64 for GEMM2) x 16 token rows, and the
+// weight scales (2 x H/128 for GEMM1, I/128 for GEMM2).  Two copies, by unit
+// parity.
+constexpr int kSmallMaxBlk = static_cast<int>(kSmallMaxScaleBlocks);
+constexpr int kSmallScaleFloats = kSmallMaxBlk * kSmallN + 2 * kSmallMaxBlk;
 
 template <int kMode>
 struct SmallCfg {
@@ -48,8 +54,8 @@ struct SmallCfg {
 
 template <int kMode>
 constexpr int small_smem_bytes() {
-  return 1024 + SmallCfg<kMode>::kStages * SmallCfg<kMode>::kStageBytes + 4096 +
-         (2 * kMaxExperts + 2) * 4;
+  return 1024 + SmallCfg<kMode>::kStages * SmallCfg<kMode>::kStageBytes +
+         2 * kSmallScaleFloats * 4 + 4096 + (2 * kMaxExperts + 2) * 4;
 }
 
 struct SmallUnit {
@@ -106,7 +112,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sW = smem;                                   // S x kWBytes (1024-aligned)
   uint8_t* sT = smem + S * Cfg::kWBytes;                // S x 2 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(sT + S * kTokBytes);
+  float* scale_s = reinterpret_cast<float*>(sT + S * kTokBytes);   // [2][kSmallScaleFloats]
+  uint64_t* full = reinterpret_cast<uint64_t*>(scale_s + 2 * kSmallScaleFloats);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + kSmallBufs;
@@ -273,39 +280,43 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t g = 0;
     uint32_t ephase = 0;
+    uint32_t unit_parity = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
       const SmallUnit c = decode_small(u, ustart_s, counts_s, tstart_s, E, NT);
       constexpr int kAcc = kMode == kGemm1 ? 2 * kSmallN : kSmallN;
       float acc[kAcc];
 #pragma unroll
       for (int i = 0; i < kAcc; ++i) acc[i] = 0.f;
-      const float* sa_p = p.a_scale + c.row0;      // + block * npad: 16 contiguous scales
+      // Stage the unit's scales: one round of loads per unit instead of a
+      // dependent global load per K block.  The copy used alternates with the
+      // unit parity; the barrier below also guarantees that no warp still reads
+      // the copy the next-but-one unit overwrites.
+      float* sc = scale_s + (unit_parity & 1u) * kSmallScaleFloats;
+      float* sc_w = sc + kSmallMaxBlk * kSmallN;
+      ++unit_parity;
+      {
+        const int nblk = kMode == kGemm1 ? KB : 2 * KB;
+        for (int i = threadIdx.x; i < nblk * kSmallN; i += 128)
+          sc[i] = __ldg(p.a_scale + static_cast<int64_t>(i >> 4) * p.npad + c.row0 + (i & 15));
+        if constexpr (kMode == kGemm1) {
+          // W1 scale [E, 2I/128, H/128]: X1 block n, X2 block I/128 + n.
+          const int ib = p.inter / kBlockK;
+          const float* ws_x1 = p.b_scale + (static_cast<int64_t>(c.e) * 2 * ib + c.n) * KB;
+          for (int i = threadIdx.x; i < 2 * KB; i += 128)
+            sc_w[i] = __ldg(ws_x1 + (i < KB ? i : static_cast<int64_t>(ib) * KB + i - KB));
+        } else {
+          // W2 scale [E, H/128, I/128].
+          const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * (p.hidden / kBlockK) + c.n) * KB;
+          for (int i = threadIdx.x; i < KB; i += 128) sc_w[i] = __ldg(ws + i);
+        }
+        if (!epi_sync(ebar, ephase, lane, abort_flag, p.ctrl)) goto epi_done;
+      }
       if constexpr (kMode == kGemm1) {
-        // W1 scale [E, 2I/128, H/128]: X1 block n, X2 block I/128 + n.
-        const int ib = p.inter / kBlockK;
-        const float* ws_x1 = p.b_scale + (static_cast<int64_t>(c.e) * 2 * ib + c.n) * KB;
-        const float* ws_x2 = ws_x1 + static_cast<int64_t>(ib) * KB;
         // Groups are consumed kBatch1 at a time: all their TMEM loads go out
         // before one tcgen05.wait::ld, so a batch costs one TMEM round trip.
-        // The batch's scales are requested before its barrier waits.
         constexpr int kBatch1 = 2;
         for (int kb0 = 0; kb0 < KB; kb0 += kBatch1) {
-          float sa[kBatch1][kSmallN], w1[kBatch1], w2[kBatch1];
           uint32_t bufs[kBatch1];
-#pragma unroll
-          for (int bi = 0; bi < kBatch1; ++bi) {
-            const int kb = kb0 + bi;
-            if (kb < KB) {
-              const float4* s4 = reinterpret_cast<const float4*>(sa_p + static_cast<int64_t>(kb) * p.npad);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float4 f = __ldg(s4 + j);
-                sa[bi][4 * j] = f.x; sa[bi][4 * j + 1] = f.y; sa[bi][4 * j + 2] = f.z; sa[bi][4 * j + 3] = f.w;
-              }
-              w1[bi] = __ldg(ws_x1 + kb);
-              w2[bi] = __ldg(ws_x2 + kb);
-            }
-          }
 #pragma unroll
           for (int bi = 0; bi < kBatch1; ++bi) {
             const uint32_t gg = g + bi;
@@ -327,11 +338,20 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             if (kb0 + bi < KB && lane == 0) mbar_arrive(&tempty[bufs[bi]]);
 #pragma unroll
           for (int bi = 0; bi < kBatch1; ++bi) {
-            if (kb0 + bi < KB) {
+            const int kb = kb0 + bi;
+            if (kb < KB) {
+              const float w1 = sc_w[kb], w2 = sc_w[KB + kb];
+              const float4* s4 = reinterpret_cast<const float4*>(sc + kb * kSmallN);
 #pragma unroll
-              for (int j = 0; j < kSmallN; ++j) {
-                acc[j] = fmaf(v[bi][j], sa[bi][j] * w1[bi], acc[j]);
-                acc[kSmallN + j] = fmaf(v[bi][kSmallN + j], sa[bi][j] * w2[bi], acc[kSmallN + j]);
+              for (int j4 = 0; j4 < 4; ++j4) {
+                const float4 f = s4[j4];
+                const float sa[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                  const int j = 4 * j4 + jj;
+                  acc[j] = fmaf(v[bi][j], sa[jj] * w1, acc[j]);
+                  acc[kSmallN + j] = fmaf(v[bi][kSmallN + j], sa[jj] * w2, acc[kSmallN + j]);
+                }
               }
               ++g;
             }
@@ -367,28 +387,12 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         // red_s is rewritten by the next unit
         if (!epi_sync(ebar, ephase, lane, abort_flag, p.ctrl)) goto epi_done;
       } else {
-        // W2 scale [E, H/128, I/128]; intermediate scales [I/64, npad].
-        const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * (p.hidden / kBlockK) + c.n) * KB;
         // Scale groups (two per K block) are consumed kBatch2 at a time, as in
         // GEMM1.
         constexpr int kBatch2 = 4;
         const int ngroups = 2 * KB;
         for (int g0 = 0; g0 < ngroups; g0 += kBatch2) {
-          float sa[kBatch2][kSmallN], sw[kBatch2];
           uint32_t bufs[kBatch2];
-#pragma unroll
-          for (int bi = 0; bi < kBatch2; ++bi) {
-            const int gi = g0 + bi;
-            if (gi < ngroups) {
-              const float4* s4 = reinterpret_cast<const float4*>(sa_p + static_cast<int64_t>(gi) * p.npad);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float4 f = __ldg(s4 + j);
-                sa[bi][4 * j] = f.x; sa[bi][4 * j + 1] = f.y; sa[bi][4 * j + 2] = f.z; sa[bi][4 * j + 3] = f.w;
-              }
-              sw[bi] = __ldg(ws + (gi >> 1));
-            }
-          }
 #pragma unroll
           for (int bi = 0; bi < kBatch2; ++bi) {
             const uint32_t gg = g + bi;
@@ -410,9 +414,18 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             if (g0 + bi < ngroups && lane == 0) mbar_arrive(&tempty[bufs[bi]]);
 #pragma unroll
           for (int bi = 0; bi < kBatch2; ++bi) {
-            if (g0 + bi < ngroups) {
+            const int gi = g0 + bi;
+            if (gi < ngroups) {
+              const float sw = sc_w[gi >> 1];
+              const float4* s4 = reinterpret_cast<const float4*>(sc + gi * kSmallN);
 #pragma unroll
-              for (int j = 0; j < kSmallN; ++j) acc[j] = fmaf(v[bi][j], sa[bi][j] * sw[bi], acc[j]);
+              for (int j4 = 0; j4 < 4; ++j4) {
+                const float4 f = s4[j4];
+                acc[4 * j4] = fmaf(v[bi][4 * j4], f.x * sw, acc[4 * j4]);
+                acc[4 * j4 + 1] = fmaf(v[bi][4 * j4 + 1], f.y * sw, acc[4 * j4 + 1]);
+                acc[4 * j4 + 2] = fmaf(v[bi][4 * j4 + 2], f.z * sw, acc[4 * j4 + 2]);
+                acc[4 * j4 + 3] = fmaf(v[bi][4 * j4 + 3], f.w * sw, acc[4 * j4 + 3]);
+              }
               ++g;
             }
           }

@@ -99,6 +99,8 @@ int launch_gemm(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, cons
 // The forward takes the decode-shaped GEMMs when T * top_k <= this many rows
 // per routed expert on average.
 constexpr int64_t kSmallPathMaxAvgRows = 4;
+// ... and when a unit's scale blocks (H/128, I/64) fit its shared-memory stage.
+constexpr int64_t kSmallMaxScaleBlocks = 64;
 
 // Decode-shaped variant with swapped operands (moe_gemm_small.cu): weight rows
 // are the M=128 operand, 16 permuted token rows the N operand.  n_tiles counts

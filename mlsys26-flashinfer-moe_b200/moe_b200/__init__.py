@@ -5,6 +5,8 @@
 ``include/moe_b200.h``).
 """
 from .api import run, build_args, forward_args, workspace_views, device_error  # noqa: F401
+from .graph import LayerGraph  # noqa: F401
 from . import workloads  # noqa: F401
 
-__all__ = ["run", "build_args", "forward_args", "workspace_views", "device_error", "workloads"]
+__all__ = ["run", "build_args", "forward_args", "workspace_views", "device_error", "LayerGraph",
+           "workloads"]

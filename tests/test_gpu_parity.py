@@ -155,6 +155,27 @@ def test_decode_path_skewed_routing(cuda_device, t, e_local, zipf):
     np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.parametrize("t", [1, 8])
+def test_layer_graph_replay(cuda_device, t):
+    """A captured forward equals the eager one, also after new step inputs are
+    copied into the captured tensors."""
+    from moe_b200 import LayerGraph, run
+    inp, shape = dsv3_inputs(t, seed=40 + t, e_local=32)
+    out_g = torch.empty(t, shape.hidden, dtype=torch.bfloat16, device="cuda")
+    graph = LayerGraph(*workloads.run_args(inp), out_g, n_group=8, topk_group=4, top_k=8)
+    for step in range(2):
+        nxt = workloads.make_inputs(shape, seed=80 + 10 * step + t, device="cuda", weights=False)
+        graph.set_inputs(nxt["routing_logits"], nxt["hidden_states"], nxt["hidden_states_scale"])
+        graph.replay()
+        eager_args = workloads.run_args(inp)
+        eager_args[0], eager_args[2], eager_args[3] = (nxt["routing_logits"], nxt["hidden_states"],
+                                                       nxt["hidden_states_scale"])
+        out_e = torch.empty_like(out_g)
+        run(*eager_args, out_e)
+        torch.cuda.synchronize()
+        assert (out_g.float() - out_e.float()).abs().max().item() <= 2e-3
+
+
 def test_zero_tokens_is_a_noop(cuda_device):
     inp, shape = dsv3_inputs(0, seed=1, e_local=32)
     out, _, _ = run_cuda(inp, shape)
