@@ -162,6 +162,19 @@ int moe_fp8_route_noalloc(const float* routing_logits, const void* routing_bias,
                           int32_t* topk_idx, float* topk_weights, int32_t* expert_counts,
                           void* stream);
 
+/* bf16 -> FP8 e4m3 quantisation of activations with one fp32 scale per token
+ * and 128 columns: x [T, H] bf16 (row-major) -> q [T, H] e4m3 and
+ * scale [H/128, T] fp32, scale = max(amax * fp32(1/448), 1e-12),
+ * q = e4m3_rne(x / scale) (saturating) -- the values torch produces for
+ * max(amax / 448, 1e-12) and (x / scale).to(float8_e4m3fn).  Produces the forward's hidden_states / hidden_states_scale in the
+ * layout run() asserts (reference kernel.py:603); the reference itself receives
+ * them already quantised, so this replaces the quantisation step of its callers
+ * (the FlashInfer-Bench workloads; the expert-parallel layer's bf16 inputs).
+ * H must be a multiple of 128, x and q 16-byte aligned.  Asynchronous on
+ * `stream`, no allocation. */
+int moe_bf16_to_fp8_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale,
+                          void* stream);
+
 /* Human-readable name of a status code. */
 const char* moe_fp8_status_string(int code);
 

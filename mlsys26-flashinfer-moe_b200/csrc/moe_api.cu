@@ -427,6 +427,19 @@ const char* moe_fp8_status_string(int code) {
   }
 }
 
+int moe_bf16_to_fp8_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale,
+                          void* stream) {
+  if (T < 0 || H <= 0 || H % 128 != 0) return MOE_ERR_SHAPE;
+  if (T == 0) return MOE_OK;
+  if (!x || !q || !scale) return MOE_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u) != 0)
+    return MOE_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  const int st = device_info(&dev);
+  if (st) return st;
+  return launch_quant_1x128(x, T, H, q, scale, dev->sms, static_cast<cudaStream_t>(stream));
+}
+
 int moe_fp8_num_sms(int device, int32_t* out) {
   if (!out) return MOE_ERR_INVALID_ARG;
   int v = 0;

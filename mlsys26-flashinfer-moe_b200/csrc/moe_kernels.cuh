@@ -109,6 +109,10 @@ int gemm_small_set_smem_attrs();
 int launch_gemm_small(int mode, const CUtensorMap& tm_w, const CUtensorMap& tm_tok,
                       const GemmParams& p, int grid, cudaStream_t stream);
 
+// bf16 -> e4m3 1x128 activation quantisation (moe_quant.cu).
+int launch_quant_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale, int sms,
+                       cudaStream_t stream);
+
 constexpr int gemm_smem_bytes() {
   return 1024 /*alignment slack*/ + kStages * kStageBytes + kXposeBytes +
          4096 /*barriers + tables*/;

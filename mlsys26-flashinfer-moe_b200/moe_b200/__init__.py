@@ -4,9 +4,10 @@
 (``kernel.py:562``); the kernels live in ``libmoe_b200.so`` (C ABI in
 ``include/moe_b200.h``).
 """
-from .api import run, build_args, forward_args, workspace_views, device_error  # noqa: F401
+from .api import (run, build_args, forward_args, workspace_views, device_error,  # noqa: F401
+                  quantize_1x128)
 from .graph import LayerGraph  # noqa: F401
 from . import workloads  # noqa: F401
 
-__all__ = ["run", "build_args", "forward_args", "workspace_views", "device_error", "LayerGraph",
+__all__ = ["run", "build_args", "forward_args", "workspace_views", "device_error", "quantize_1x128", "LayerGraph",
            "workloads"]

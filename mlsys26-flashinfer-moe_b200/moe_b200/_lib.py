@@ -97,6 +97,8 @@ SYMBOLS = {
                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                              ctypes.c_int64, ctypes.c_float, ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "moe_bf16_to_fp8_1x128": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "moe_fp8_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "moe_fp8_num_sms": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int32)]),
 }

@@ -180,6 +180,31 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     return None
 
 
+def quantize_1x128(x: torch.Tensor, q: Optional[torch.Tensor] = None,
+                   scale: Optional[torch.Tensor] = None):
+    """bf16 ``[T, H]`` CUDA activations -> (e4m3 ``[T, H]``, fp32 ``[H/128, T]``) on the
+    current stream: ``scale = max(amax/448, 1e-12)`` per token and 128 columns and
+    ``q = e4m3(x / scale)``, the layout ``run()`` takes as ``hidden_states`` /
+    ``hidden_states_scale`` (reference ``kernel.py:603``)."""
+    assert x.dtype == torch.bfloat16 and x.dim() == 2, "x must be a bf16 [T, H] tensor"
+    assert x.is_cuda, "x must be a CUDA tensor"
+    x = x.contiguous()
+    t, h = x.shape
+    assert h % 128 == 0, "H must be a multiple of 128"
+    if q is None:
+        q = torch.empty(t, h, dtype=_F8, device=x.device)
+    if scale is None:
+        scale = torch.empty(h // 128, t, dtype=torch.float32, device=x.device)
+    assert q.shape == (t, h) and q.dtype == _F8 and q.is_contiguous()
+    assert scale.shape == (h // 128, t) and scale.dtype == torch.float32 and scale.is_contiguous()
+    stream = torch.cuda.current_stream(x.device)
+    code = _lib.load().moe_bf16_to_fp8_1x128(x.data_ptr(), t, h, q.data_ptr(), scale.data_ptr(),
+                                            ctypes.c_void_p(stream.cuda_stream))
+    if code:
+        _raise(code, "moe_bf16_to_fp8_1x128")
+    return q, scale
+
+
 def device_error(args: _lib.MoeFwdArgs, stream: Optional[torch.cuda.Stream] = None):
     """(code, info) of the device-side error word of the last forward on the
     workspace in ``args``; blocks on the stream."""

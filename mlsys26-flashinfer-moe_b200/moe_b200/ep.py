@@ -148,3 +148,15 @@ def ep_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale,
         timings["rows_sent"] = len(send_tok)
         timings["rows_received"] = n_recv
     return output
+
+
+def ep_forward_bf16(routing_logits, routing_bias, hidden_states_bf16, gemm1_weights,
+                    gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                    routed_scaling_factor, output, **kw):
+    """``ep_forward`` for a layer that starts from bf16 activations: this rank's
+    tokens are quantised to e4m3 with 1x128 scales on the GPU
+    (``moe_bf16_to_fp8_1x128``) before routing, so only FP8 rows and their scales
+    cross NVLink in the dispatch."""
+    hs, hss = api.quantize_1x128(hidden_states_bf16)
+    return ep_forward(routing_logits, routing_bias, hs, hss, gemm1_weights, gemm1_weights_scale,
+                      gemm2_weights, gemm2_weights_scale, routed_scaling_factor, output, **kw)

@@ -1,8 +1,11 @@
-"""Expert parallelism on 2 GPUs over NCCL (skipped with fewer GPUs).
+"""Expert parallelism over NCCL: one rank (any GPU box) and two ranks (skipped
+with fewer GPUs).
 
-Each rank holds half of the 256 experts and its own tokens; the layer output of
+Each rank holds 256/W of the experts and its own tokens; the layer output of
 every rank's tokens must match the single-GPU kernel with all experts on that
-GPU, within the output tolerance (partials travel as bf16).
+GPU, within the output tolerance (partials travel as bf16).  The bf16 variants
+start from bf16 activations (``ep_forward_bf16``, config 4) and compare with the
+same activations quantised by ``quantize_1x128`` and run on one GPU.
 """
 import os
 import socket
@@ -23,13 +26,13 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, bf16=False):
     import datetime
     import sys
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(repo, "mlsys26-flashinfer-moe_b200"))
     import torch.distributed as dist
-    from moe_b200 import ep, run, workloads
+    from moe_b200 import ep, quantize_1x128, run, workloads
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
@@ -45,10 +48,17 @@ def _worker(rank, world, port, out_dir):
     lo, per = ep.expert_range(rank, world, 256)
     sl = slice(lo, lo + per)
     out = torch.empty(t, 512, dtype=torch.bfloat16, device="cuda")
-    ep.ep_forward(tok["routing_logits"], tok["routing_bias"], tok["hidden_states"],
-                  tok["hidden_states_scale"], wts["gemm1_weights"][sl].contiguous(),
-                  wts["gemm1_weights_scale"][sl].contiguous(), wts["gemm2_weights"][sl].contiguous(),
-                  wts["gemm2_weights_scale"][sl].contiguous(), 2.5, out)
+    shard = (wts["gemm1_weights"][sl].contiguous(), wts["gemm1_weights_scale"][sl].contiguous(),
+             wts["gemm2_weights"][sl].contiguous(), wts["gemm2_weights_scale"][sl].contiguous())
+    if bf16:
+        g = torch.Generator(device="cuda")
+        g.manual_seed(70 + rank)
+        x = torch.randn(t, 512, generator=g, device="cuda").to(torch.bfloat16)
+        ep.ep_forward_bf16(tok["routing_logits"], tok["routing_bias"], x, *shard, 2.5, out)
+        tok["hidden_states"], tok["hidden_states_scale"] = quantize_1x128(x)
+    else:
+        ep.ep_forward(tok["routing_logits"], tok["routing_bias"], tok["hidden_states"],
+                      tok["hidden_states_scale"], *shard, 2.5, out)
     ref = torch.empty_like(out)
     run(tok["routing_logits"], tok["routing_bias"], tok["hidden_states"],
         tok["hidden_states_scale"], wts["gemm1_weights"], wts["gemm1_weights_scale"],
@@ -60,14 +70,24 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_ep_two_gpus_match_single_gpu(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
-    for r in range(2):
+def _check(tmp_path, world):
+    for r in range(world):
         d = np.load(tmp_path / f"gpu_rank{r}.npz")
         assert np.isfinite(d["out"]).all()
         np.testing.assert_allclose(d["out"], d["ref"], atol=1e-2, rtol=2e-2)
         cos = float((d["out"] * d["ref"]).sum() /
                     (np.linalg.norm(d["out"]) * np.linalg.norm(d["ref"])))
         assert cos >= 0.9999
+
+
+def test_ep_one_gpu_from_bf16(tmp_path, cuda_device):
+    mp.spawn(_worker, args=(1, _free_port(), str(tmp_path), True), nprocs=1, join=True)
+    _check(tmp_path, 1)
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_ep_two_gpus_match_single_gpu(tmp_path, bf16):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), bf16), nprocs=2, join=True)
+    _check(tmp_path, 2)
