@@ -175,6 +175,60 @@ int moe_fp8_route_noalloc(const float* routing_logits, const void* routing_bias,
 int moe_bf16_to_fp8_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale,
                           void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Expert-parallel layer with the token exchange done over NVLink peer memory.
+ *
+ * No counterpart function exists in the reference: its API expresses one shard
+ * (local_expert_offset + a contiguous weight slice, kernel.py:572) and leaves
+ * the exchange of tokens between shards to the caller.  One process per GPU;
+ * rank r of `world` owns experts [r*E/world, (r+1)*E/world) and up to T_max
+ * tokens.  Each rank's receive buffers are mapped into every peer with CUDA
+ * IPC; the caller moves the 64-byte handles (moe_ep_ipc_handle, e.g. with an
+ * all-gather of bytes) and passes all of them to moe_ep_connect.  Per forward,
+ * in this order on one stream per rank, with the caller's collectives between:
+ *   moe_ep_send_plan   route own tokens; send_cnt[world] = rows for each rank
+ *   (all-gather send_cnt of every rank into cnt_all[world][world], source-major)
+ *   moe_ep_dispatch    store FP8 rows, scales and logits into the owners' buffers
+ *   (barrier across ranks)
+ *   moe_ep_experts     local experts on the received rows; bf16 partials stored
+ *                      back into the sources' buffers
+ *   (barrier across ranks)
+ *   moe_ep_finalize    sum of a token's partials in rank order -> bf16 output
+ * The routing bias must be the same on every rank. */
+typedef struct MoeEpConfig {
+  int32_t world, rank;
+  int64_t T_max;             /* most tokens any rank passes in one forward, < 2^24 */
+  int64_t H, I, E_global, n_group, topk_group, top_k;
+} MoeEpConfig;
+
+typedef struct MoeEp MoeEp;
+
+/* Allocates this rank's receive region (world*T_max rows) and workspaces on the
+ * current device. */
+int moe_ep_create(const MoeEpConfig* cfg, MoeEp** out);
+/* 64-byte CUDA IPC handle of this rank's receive region. */
+int moe_ep_ipc_handle(MoeEp* ep, void* handle_out);
+/* all_handles: world consecutive 64-byte handles, rank order. */
+int moe_ep_connect(MoeEp* ep, const void* all_handles);
+int moe_ep_send_plan(MoeEp* ep, const float* routing_logits, const void* routing_bias,
+                     int32_t bias_dtype, int64_t T, float routed_scaling_factor,
+                     int32_t* send_cnt, void* stream);
+/* hidden_states [T, H] e4m3, hidden_states_scale [H/128, T], routing_logits [T, E]. */
+int moe_ep_dispatch(MoeEp* ep, const void* hidden_states, const float* hidden_states_scale,
+                    const float* routing_logits, int64_t T, const int32_t* cnt_all,
+                    void* stream);
+/* Weights: this rank's contiguous expert slice, reference layouts. */
+int moe_ep_experts(MoeEp* ep, const void* routing_bias, int32_t bias_dtype,
+                   float routed_scaling_factor, const void* gemm1_weights,
+                   const float* gemm1_weights_scale, const void* gemm2_weights,
+                   const float* gemm2_weights_scale, const int32_t* cnt_all, void* stream);
+/* output [T, H] bf16. */
+int moe_ep_finalize(MoeEp* ep, int64_t T, void* output, void* stream);
+/* First non-zero error word of the handle's kernels (blocks on `stream`). */
+int moe_ep_device_error(MoeEp* ep, void* stream, int32_t* code, int32_t* info);
+/* Unmaps peers and frees this rank's buffers (synchronises the device). */
+int moe_ep_destroy(MoeEp* ep);
+
 /* Human-readable name of a status code. */
 const char* moe_fp8_status_string(int code);
 

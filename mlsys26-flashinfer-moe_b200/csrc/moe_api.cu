@@ -212,7 +212,8 @@ T* ws_ptr(const MoeFwdArgs* a, size_t off) {
   return reinterpret_cast<T*>(static_cast<uint8_t*>(a->workspace) + off);
 }
 
-int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
+int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
+                 const int* T_dev = nullptr) {
   const MoeWorkspaceLayout& w = L.w;
   RouteParams rp{};
   rp.logits = a->routing_logits;
@@ -236,6 +237,7 @@ int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s) {
   rp.counts = ws_ptr<int>(a, w.counts);
   rp.tile_start = ws_ptr<int>(a, w.tile_start);
   rp.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
+  rp.T_dev = T_dev;
   if (cudaMemsetAsync(rp.ctrl, 0, sizeof(CtrlBlock), s) != cudaSuccess) return MOE_ERR_CUDA;
   moe_route_kernel<<<L.blocks, kRouteThreads, 0, s>>>(rp);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
@@ -246,8 +248,12 @@ int record(void* const* ev, int i, cudaStream_t s) {
   return cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
+// T_dev (expert-parallel receive side): the row count lives on the device and
+// a->T is only its capacity; the fp32 accumulator rows are zeroed by the
+// permute kernel for exactly the rows that exist, and the layer stops after
+// GEMM2 (the caller combines the fp32 rows).
 int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
-                   void* const* ev = nullptr) {
+                   void* const* ev = nullptr, const int* T_dev = nullptr) {
   DeviceInfo* dev = nullptr;
   int st = device_info(&dev);
   if (st) return st;
@@ -255,8 +261,9 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   const MoeWorkspaceLayout& w = L.w;
   const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local;
   float* out_f32 = ws_ptr<float>(a, w.out_f32);
-  if (cudaMemsetAsync(out_f32, 0, sizeof(float) * T * H, s) != cudaSuccess) return MOE_ERR_CUDA;
-  st = launch_route(a, L, s);
+  if (!T_dev && cudaMemsetAsync(out_f32, 0, sizeof(float) * T * H, s) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  st = launch_route(a, L, s, T_dev);
   if (st) return st;
   if ((st = record(ev, 1, s))) return st;
 
@@ -274,6 +281,9 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   pp.tile_start = ws_ptr<int>(a, w.tile_start);
   pp.hidden = static_cast<const uint8_t*>(a->hidden_states);
   pp.hs_scale = a->hidden_states_scale;
+  pp.scale_ld = T;
+  pp.T_dev = T_dev;
+  pp.zero_rows = T_dev ? out_f32 : nullptr;
   pp.row_token = ws_ptr<int>(a, w.row_token);
   pp.row_weight = ws_ptr<float>(a, w.row_weight);
   pp.a_perm = ws_ptr<uint8_t>(a, w.a_perm);
@@ -334,6 +344,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
     return st;
   }
   if ((st = record(ev, 4, s))) return st;
+  if (T_dev) return MOE_OK;
 
   const int64_t n8 = T * H / 8;
   int blocks = static_cast<int>((n8 + 255) / 256);
@@ -344,6 +355,43 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
 }
 
 }  // namespace
+
+int forward_device_rows(const MoeFwdArgs* a, const int* T_dev, cudaStream_t s) {
+  int st = validate_shape(a);
+  if (st) return st;
+  const Layout L = make_layout(a);
+  if (a->T == 0) return MOE_OK;
+  if (!a->workspace || a->workspace_bytes < L.w.total_bytes) return MOE_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return MOE_ERR_ALIGNMENT;
+  return launch_forward(a, L, s, nullptr, T_dev);
+}
+
+int validate_shape_public(const MoeFwdArgs* a) { return validate_shape(a); }
+
+int route_only(const MoeFwdArgs* a, cudaStream_t s) {
+  int st = validate_shape(a);
+  if (st) return st;
+  const Layout L = make_layout(a);
+  if (a->T == 0) return MOE_OK;
+  if (!a->routing_logits || !a->routing_bias) return MOE_ERR_INVALID_ARG;
+  if (!a->workspace || a->workspace_bytes < L.w.total_bytes) return MOE_ERR_WORKSPACE;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev))) return st;
+  return launch_route(a, L, s);
+}
+
+int num_sms(int* out) {
+  DeviceInfo* dev = nullptr;
+  const int st = device_info(&dev);
+  if (st) return st;
+  *out = dev->sms;
+  return MOE_OK;
+}
+
+size_t workspace_bytes_for(const MoeFwdArgs* a) { return make_layout(a).w.total_bytes; }
+
+MoeWorkspaceLayout workspace_layout_for(const MoeFwdArgs* a) { return make_layout(a).w; }
+
 }  // namespace moe
 
 using namespace moe;

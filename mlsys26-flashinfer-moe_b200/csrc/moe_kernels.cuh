@@ -43,6 +43,7 @@ struct RouteParams {
   int* counts;       // [E_local]
   int* tile_start;   // [E_local + 1]
   CtrlBlock* ctrl;
+  const int* T_dev;  // when set, the number of rows is min(*T_dev, T) (expert-parallel receive side)
 };
 
 struct PermuteParams {
@@ -54,10 +55,13 @@ struct PermuteParams {
   const int* tile_start;
   const uint8_t* hidden;
   const float* hs_scale;
+  int64_t scale_ld;    // row stride of hs_scale [H/128, scale_ld] (T on the single-GPU path)
   int* row_token;
   float* row_weight;
   uint8_t* a_perm;
   float* a_scale_perm;
+  const int* T_dev;    // as RouteParams::T_dev
+  float* zero_rows;    // when set, rows t of this [T, H] fp32 buffer are zeroed for every token
 };
 
 // One persistent grouped GEMM launch.  Work units are (expert tile, N tile)
@@ -108,6 +112,19 @@ constexpr int64_t kSmallMaxScaleBlocks = 64;
 int gemm_small_set_smem_attrs();
 int launch_gemm_small(int mode, const CUtensorMap& tm_w, const CUtensorMap& tm_tok,
                       const GemmParams& p, int grid, cudaStream_t stream);
+
+// The layer forward of moe_api.cu with a device-resident row count (a->T is
+// the capacity): route, permute (zeroing the fp32 accumulator rows), GEMM1,
+// GEMM2 into the workspace's out_f32; no memset of the whole accumulator and no
+// bf16 finalize.  Used by the expert-parallel receive side (moe_ep.cu).
+int forward_device_rows(const MoeFwdArgs* a, const int* T_dev, cudaStream_t s);
+size_t workspace_bytes_for(const MoeFwdArgs* a);
+int validate_shape_public(const MoeFwdArgs* a);
+// Router + expert histogram only, into a->workspace (layout of a full forward).
+int route_only(const MoeFwdArgs* a, cudaStream_t s);
+// SM count of the current device (checks that it is an sm_100 part).
+int num_sms(int* out);
+MoeWorkspaceLayout workspace_layout_for(const MoeFwdArgs* a);
 
 // bf16 -> e4m3 1x128 activation quantisation (moe_quant.cu).
 int launch_quant_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale, int sms,

@@ -144,8 +144,9 @@ __device__ __forceinline__ void route_block_tokens(const RouteParams& p, int* hi
     const int e = lane * EPL + j;
     bias[j] = e < p.E ? load_bias(p.bias, p.bias_dtype, e) : 0.f;
   }
+  const int T = p.T_dev ? min(p.T, *p.T_dev) : p.T;
   const int t0 = blockIdx.x * p.tokens_per_block;
-  const int t1 = min(p.T, t0 + p.tokens_per_block);
+  const int t1 = min(T, t0 + p.tokens_per_block);
   for (int t = t0 + warp; t < t1; t += kRouteThreads / 32) route_one_token<EPL>(p, t, lane, bias, hist_s);
 }
 
@@ -211,8 +212,9 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
   __shared__ int rows_s[kMaxTokensPerBlock * kMaxTopK];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.x;
+  const int T = p.T_dev ? min(p.T, *p.T_dev) : p.T;
   const int t0 = b * p.tokens_per_block;
-  const int t1 = min(p.T, t0 + p.tokens_per_block);
+  const int t1 = min(T, t0 + p.tokens_per_block);
   for (int i = tid; i < p.E_local; i += kRouteThreads)
     cursor[i] = kTileM * p.tile_start[i] + p.block_base[static_cast<int64_t>(b) * p.E_local + i];
   __syncthreads();
@@ -240,7 +242,12 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
     p.row_weight[row] = p.topk_weights[static_cast<int64_t>(t) * p.top_k + j % p.top_k];
     for (int kb = 0; kb < hb; ++kb)
       p.a_scale_perm[static_cast<int64_t>(kb) * p.npad + row] =
-          __ldg(p.hs_scale + static_cast<int64_t>(kb) * p.T + t);
+          __ldg(p.hs_scale + static_cast<int64_t>(kb) * p.scale_ld + t);
+  }
+  if (p.zero_rows) {
+    const int64_t n4 = static_cast<int64_t>(t1 - t0) * p.H / 4;
+    float4* z = reinterpret_cast<float4*>(p.zero_rows + static_cast<int64_t>(t0) * p.H);
+    for (int64_t i = tid; i < n4; i += kRouteThreads) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   // FP8 rows: one warp per assignment, 16-byte vectors.
   const int vec = p.H / 16;

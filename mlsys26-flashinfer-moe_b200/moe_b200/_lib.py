@@ -80,6 +80,14 @@ class MoeWorkspaceLayout(ctypes.Structure):
 
 
 # Every symbol include/moe_b200.h declares, with its ctypes signature.
+class MoeEpConfig(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("T_max", ctypes.c_int64),
+                ("H", ctypes.c_int64), ("I", ctypes.c_int64), ("E_global", ctypes.c_int64),
+                ("n_group", ctypes.c_int64), ("topk_group", ctypes.c_int64),
+                ("top_k", ctypes.c_int64)]
+
+
+_VP = ctypes.c_void_p
 SYMBOLS = {
     "moe_fp8_workspace_size": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs),
                                               ctypes.POINTER(ctypes.c_size_t)]),
@@ -99,6 +107,18 @@ SYMBOLS = {
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "moe_bf16_to_fp8_1x128": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "moe_ep_create": (ctypes.c_int, [ctypes.POINTER(MoeEpConfig), ctypes.POINTER(_VP)]),
+    "moe_ep_ipc_handle": (ctypes.c_int, [_VP, _VP]),
+    "moe_ep_connect": (ctypes.c_int, [_VP, ctypes.c_char_p]),
+    "moe_ep_send_plan": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int32, ctypes.c_int64,
+                                        ctypes.c_float, _VP, _VP]),
+    "moe_ep_dispatch": (ctypes.c_int, [_VP, _VP, _VP, _VP, ctypes.c_int64, _VP, _VP]),
+    "moe_ep_experts": (ctypes.c_int, [_VP, _VP, ctypes.c_int32, ctypes.c_float, _VP, _VP, _VP,
+                                      _VP, _VP, _VP]),
+    "moe_ep_finalize": (ctypes.c_int, [_VP, ctypes.c_int64, _VP, _VP]),
+    "moe_ep_device_error": (ctypes.c_int, [_VP, _VP, ctypes.POINTER(ctypes.c_int32),
+                                           ctypes.POINTER(ctypes.c_int32)]),
+    "moe_ep_destroy": (ctypes.c_int, [_VP]),
     "moe_fp8_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "moe_fp8_num_sms": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int32)]),
 }

@@ -160,3 +160,110 @@ def ep_forward_bf16(routing_logits, routing_bias, hidden_states_bf16, gemm1_weig
     hs, hss = api.quantize_1x128(hidden_states_bf16)
     return ep_forward(routing_logits, routing_bias, hs, hss, gemm1_weights, gemm1_weights_scale,
                       gemm2_weights, gemm2_weights_scale, routed_scaling_factor, output, **kw)
+
+
+class FusedEP:
+    """Expert-parallel layer whose dispatch and combine are this library's own
+    kernels storing over NVLink into peer ranks' buffers (``moe_ep_*`` in
+    ``include/moe_b200.h``); NCCL only all-gathers the per-rank row counts
+    (``world*world`` ints, on the device) and orders the phases.
+
+    Build once per process group and layer shape (collective: every rank calls
+    it together), then call ``forward`` on every rank with its own tokens.
+    """
+
+    def __init__(self, t_max: int, hidden: int, inter: int, e_global: int = 256, *,
+                 n_group: int = 8, topk_group: int = 4, top_k: int = 8, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.t_max, self.hidden, self.inter, self.e_global = t_max, hidden, inter, e_global
+        self.n_group, self.topk_group, self.top_k = n_group, topk_group, top_k
+        self.lo, self.per = expert_range(self.rank, self.world, e_global)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        cfg = _lib.MoeEpConfig(self.world, self.rank, t_max, hidden, inter, e_global, n_group,
+                               topk_group, top_k)
+        h = ctypes.c_void_p()
+        code = lib.moe_ep_create(ctypes.byref(cfg), ctypes.byref(h))
+        if code:
+            api._raise(code, "moe_ep_create")
+        self._h = h
+        handle = (ctypes.c_ubyte * 64)()
+        code = lib.moe_ep_ipc_handle(self._h, ctypes.cast(handle, ctypes.c_void_p))
+        if code:
+            api._raise(code, "moe_ep_ipc_handle")
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        allh = torch.empty(self.world * 64, dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        code = lib.moe_ep_connect(self._h, bytes(allh.cpu().tolist()))
+        if code:
+            api._raise(code, "moe_ep_connect")
+        dist.barrier(group=group)
+        self.send_cnt = torch.zeros(self.world, dtype=torch.int32, device=self.device)
+        self.cnt_all = torch.zeros(self.world * self.world, dtype=torch.int32, device=self.device)
+        self._bar = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def _barrier(self):
+        dist.all_reduce(self._bar, group=self.group)
+
+    @torch.no_grad()
+    def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                routed_scaling_factor, output):
+        """Same arguments as ``ep_forward`` (this rank's tokens and expert slice,
+        the layer's bias); writes bf16 ``output`` [T, H]."""
+        t, h = hidden_states.shape
+        assert t <= self.t_max and h == self.hidden, "tokens exceed T_max or hidden mismatch"
+        assert gemm1_weights.shape == (self.per, 2 * self.inter, h), "weights must be this rank's slice"
+        assert routing_logits.shape == (t, self.e_global) and routing_logits.dtype == torch.float32
+        assert hidden_states.dtype == torch.float8_e4m3fn and output.dtype == torch.bfloat16
+        assert routing_bias.dtype in api._BIAS_DTYPES
+        for x in (routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                  gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, output):
+            assert x.is_cuda and x.is_contiguous(), "tensors must be contiguous CUDA tensors"
+        lib = _lib.load()
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        bdt = api._BIAS_DTYPES[routing_bias.dtype]
+        rsf = float(routed_scaling_factor)
+
+        def chk(code, where):
+            if code:
+                api._raise(code, where)
+        chk(lib.moe_ep_send_plan(self._h, routing_logits.data_ptr(), routing_bias.data_ptr(), bdt,
+                                 t, rsf, self.send_cnt.data_ptr(), st), "moe_ep_send_plan")
+        dist.all_gather_into_tensor(self.cnt_all, self.send_cnt, group=self.group)
+        chk(lib.moe_ep_dispatch(self._h, hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
+                                routing_logits.data_ptr(), t, self.cnt_all.data_ptr(), st),
+            "moe_ep_dispatch")
+        self._barrier()
+        chk(lib.moe_ep_experts(self._h, routing_bias.data_ptr(), bdt, rsf,
+                               gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(),
+                               gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(),
+                               self.cnt_all.data_ptr(), st), "moe_ep_experts")
+        self._barrier()
+        chk(lib.moe_ep_finalize(self._h, t, output.data_ptr(), st), "moe_ep_finalize")
+        return output
+
+    def forward_bf16(self, routing_logits, routing_bias, hidden_states_bf16, *weights_and_rest):
+        """``forward`` from bf16 activations, quantised 1x128 on the GPU first."""
+        hs, hss = api.quantize_1x128(hidden_states_bf16)
+        return self.forward(routing_logits, routing_bias, hs, hss, *weights_and_rest)
+
+    def device_error(self):
+        code, info = ctypes.c_int32(0), ctypes.c_int32(0)
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        if _lib.load().moe_ep_device_error(self._h, st, ctypes.byref(code), ctypes.byref(info)):
+            raise RuntimeError("moe_ep_device_error failed")
+        return code.value, info.value
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.load().moe_ep_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -26,7 +26,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, out_dir, bf16=False):
+def _worker(rank, world, port, out_dir, bf16=False, fused=False, steps=1):
     import datetime
     import sys
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -50,7 +50,22 @@ def _worker(rank, world, port, out_dir, bf16=False):
     out = torch.empty(t, 512, dtype=torch.bfloat16, device="cuda")
     shard = (wts["gemm1_weights"][sl].contiguous(), wts["gemm1_weights_scale"][sl].contiguous(),
              wts["gemm2_weights"][sl].contiguous(), wts["gemm2_weights_scale"][sl].contiguous())
-    if bf16:
+    if fused:
+        layer = ep.FusedEP(400, 512, 256, 256)
+        for _ in range(steps):     # repeated steps reuse every exchange buffer
+            out.fill_(float("nan"))
+            if bf16:
+                g = torch.Generator(device="cuda")
+                g.manual_seed(70 + rank)
+                x = torch.randn(t, 512, generator=g, device="cuda").to(torch.bfloat16)
+                layer.forward_bf16(tok["routing_logits"], tok["routing_bias"], x, *shard, 2.5, out)
+                tok["hidden_states"], tok["hidden_states_scale"] = quantize_1x128(x)
+            else:
+                layer.forward(tok["routing_logits"], tok["routing_bias"], tok["hidden_states"],
+                              tok["hidden_states_scale"], *shard, 2.5, out)
+        torch.cuda.synchronize()
+        assert layer.device_error() == (0, 0)
+    elif bf16:
         g = torch.Generator(device="cuda")
         g.manual_seed(70 + rank)
         x = torch.randn(t, 512, generator=g, device="cuda").to(torch.bfloat16)
@@ -67,6 +82,8 @@ def _worker(rank, world, port, out_dir, bf16=False):
     np.savez(os.path.join(out_dir, f"gpu_rank{rank}.npz"), out=out.float().cpu().numpy(),
              ref=ref.float().cpu().numpy())
     dist.barrier()
+    if fused:
+        layer.close()
     dist.destroy_process_group()
 
 
@@ -86,8 +103,16 @@ def test_ep_one_gpu_from_bf16(tmp_path, cuda_device):
 
 
 @pytest.mark.parametrize("bf16", [False, True])
-def test_ep_two_gpus_match_single_gpu(tmp_path, bf16):
+def test_fused_ep_one_gpu(tmp_path, cuda_device, bf16):
+    """The NVLink dispatch/combine path with one rank (its own peer)."""
+    mp.spawn(_worker, args=(1, _free_port(), str(tmp_path), bf16, True, 3), nprocs=1, join=True)
+    _check(tmp_path, 1)
+
+
+@pytest.mark.parametrize("bf16,fused", [(False, False), (True, False), (False, True),
+                                        (True, True)])
+def test_ep_two_gpus_match_single_gpu(tmp_path, bf16, fused):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), bf16), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), bf16, fused, 3), nprocs=2, join=True)
     _check(tmp_path, 2)
