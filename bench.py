@@ -498,10 +498,16 @@ def run_ep(a):
     # NCCL only all-gathers row counts and orders the phases.
     layer = ep.FusedEP(t, shape.hidden, shape.inter, 256)
 
+    stage_names = ["send_plan", "count_allgather", "dispatch", "barrier1", "experts_combine",
+                   "barrier2", "finalize"]
+
     def step(logits, x, o, tim=None):
-        layer.forward_bf16(logits, inp["routing_bias"], x, *wts, shape.routed_scaling_factor, o)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(8)] if tim is not None else None
+        layer.forward_bf16(logits, inp["routing_bias"], x, *wts, shape.routed_scaling_factor, o,
+                           events=evs)
         if tim is not None:
             tim["send_cnt"] = layer.send_cnt
+            tim.setdefault("events", []).append(evs)
 
     dev_in = (inp["routing_logits"], x_bf16)
     for _ in range(a.warmup):
@@ -552,6 +558,12 @@ def run_ep(a):
                                       f"from the library's kernels; NCCL for counts and barriers)",
                        "l2": "weights > L2 (no flush needed)"},
             "rows_sent_rank0": int(tim["send_cnt"].sum().item()) if "send_cnt" in tim else None,
+            # rows each rank receives (sum over sources of cnt_all[source][rank]): the
+            # slowest rank sets the step time
+            "rows_received_per_rank": layer.cnt_all.view(world, world).sum(0).tolist(),
+            "stage_ms_rank0": {n: round(statistics.mean(ev[j].elapsed_time(ev[j + 1])
+                                                        for ev in tim["events"]), 4)
+                               for j, n in enumerate(stage_names)} if tim.get("events") else None,
             "clocks": clocks.summary(),
             "e2e": {"value": round(world * t / (ms2_v * 1e-3), 1), "unit": "tokens/s",
                     "ms_per_step": round(ms2_v, 4),

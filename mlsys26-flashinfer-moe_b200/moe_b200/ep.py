@@ -210,9 +210,12 @@ class FusedEP:
     @torch.no_grad()
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale,
                 gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
-                routed_scaling_factor, output):
+                routed_scaling_factor, output, events: Optional[list] = None):
         """Same arguments as ``ep_forward`` (this rank's tokens and expert slice,
-        the layer's bias); writes bf16 ``output`` [T, H]."""
+        the layer's bias); writes bf16 ``output`` [T, H].  ``events``: optional
+        list of 8 timing-enabled CUDA events recorded at the stage boundaries
+        (start, send plan, count all-gather, dispatch, barrier, experts + combine,
+        barrier, finalize)."""
         t, h = hidden_states.shape
         assert t <= self.t_max and h == self.hidden, "tokens exceed T_max or hidden mismatch"
         assert gemm1_weights.shape == (self.per, 2 * self.inter, h), "weights must be this rank's slice"
@@ -230,25 +233,39 @@ class FusedEP:
         def chk(code, where):
             if code:
                 api._raise(code, where)
+
+        def mark(i):
+            if events is not None:
+                events[i].record()
+        mark(0)
         chk(lib.moe_ep_send_plan(self._h, routing_logits.data_ptr(), routing_bias.data_ptr(), bdt,
                                  t, rsf, self.send_cnt.data_ptr(), st), "moe_ep_send_plan")
+        mark(1)
         dist.all_gather_into_tensor(self.cnt_all, self.send_cnt, group=self.group)
+        mark(2)
         chk(lib.moe_ep_dispatch(self._h, hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
                                 routing_logits.data_ptr(), t, self.cnt_all.data_ptr(), st),
             "moe_ep_dispatch")
+        mark(3)
         self._barrier()
+        mark(4)
         chk(lib.moe_ep_experts(self._h, routing_bias.data_ptr(), bdt, rsf,
                                gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(),
                                gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(),
                                self.cnt_all.data_ptr(), st), "moe_ep_experts")
+        mark(5)
         self._barrier()
+        mark(6)
         chk(lib.moe_ep_finalize(self._h, t, output.data_ptr(), st), "moe_ep_finalize")
+        mark(7)
         return output
 
-    def forward_bf16(self, routing_logits, routing_bias, hidden_states_bf16, *weights_and_rest):
+    def forward_bf16(self, routing_logits, routing_bias, hidden_states_bf16, *weights_and_rest,
+                     events: Optional[list] = None):
         """``forward`` from bf16 activations, quantised 1x128 on the GPU first."""
         hs, hss = api.quantize_1x128(hidden_states_bf16)
-        return self.forward(routing_logits, routing_bias, hs, hss, *weights_and_rest)
+        return self.forward(routing_logits, routing_bias, hs, hss, *weights_and_rest,
+                            events=events)
 
     def device_error(self):
         code, info = ctypes.c_int32(0), ctypes.c_int32(0)
