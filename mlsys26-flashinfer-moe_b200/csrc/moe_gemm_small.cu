@@ -34,8 +34,7 @@ namespace {
 constexpr int kSmallN = 16;                // token rows per unit (MMA N)
 constexpr int kSmallThreads = 192;
 constexpr int kSmallTmemCols = 256;
-constexpr int kSmallBufs = 8;              // TMEM groups of 32 columns
-constexpr int kSmallBufCols = 32;
+constexpr int kSmallBufsMax = 16;          // TMEM accumulator groups (barrier slots)
 constexpr int kTokBytes = kSmallN * kBlockK;   // 2 KB token box per K block
 // Scale blocks per unit staged in shared memory: activation / intermediate
 // scale blocks (H/128 for GEMM1, I/64 for GEMM2) x 16 token rows, and the
@@ -50,6 +49,10 @@ struct SmallCfg {
   static constexpr int kStageBytes = kWBytes + kTokBytes;
   static constexpr int kStages = kMode == kGemm1 ? 6 : 11;
   static constexpr int kGroups = kMode == kGemm1 ? 1 : 2;   // scale groups per K block
+  // TMEM groups in the 256 allocated columns: GEMM1 groups hold the X1 and X2
+  // chains (2 x 16 columns), GEMM2 groups 16 columns.
+  static constexpr int kBufCols = kMode == kGemm1 ? 2 * kSmallN : kSmallN;
+  static constexpr int kBufs = kSmallTmemCols / kBufCols;
 };
 
 template <int kMode>
@@ -116,8 +119,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(scale_s + 2 * kSmallScaleFloats);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
-  uint64_t* tempty = tfull + kSmallBufs;
-  uint64_t* drain = tempty + kSmallBufs;
+  uint64_t* tempty = tfull + kSmallBufsMax;
+  uint64_t* drain = tempty + kSmallBufsMax;
   uint64_t* ebar = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -165,7 +168,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < kSmallBufs; ++b) {
+    for (int b = 0; b < Cfg::kBufs; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4);
     }
@@ -237,11 +240,11 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
           const uint64_t td = t_desc0 + ((static_cast<uint32_t>(stage) * kTokBytes) >> 4);
 #pragma unroll
           for (int gi = 0; gi < Cfg::kGroups; ++gi, ++g) {
-            const uint32_t buf = g % kSmallBufs;
-            if (!mbar_wait(&tempty[buf], ((g / kSmallBufs) & 1u) ^ 1u, abort_flag, p.ctrl, 13))
+            const uint32_t buf = g % Cfg::kBufs;
+            if (!mbar_wait(&tempty[buf], ((g / Cfg::kBufs) & 1u) ^ 1u, abort_flag, p.ctrl, 13))
               goto mma_done;
             tc_fence_after();
-            const uint32_t d = tmem_base + buf * kSmallBufCols;
+            const uint32_t d = tmem_base + buf * Cfg::kBufCols;
             if constexpr (kMode == kGemm1) {
               uint64_t a[4], b[4], a2[4];
 #pragma unroll
@@ -281,36 +284,48 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     uint32_t g = 0;
     uint32_t ephase = 0;
     uint32_t unit_parity = 0;
+    // Copies the scales of unit cu into dst: activation / intermediate scale
+    // blocks x 16 rows, then the weight scales.
+    auto stage_scales = [&](const SmallUnit& cu, float* dst) {
+      float* dst_w = dst + kSmallMaxBlk * kSmallN;
+      const int nblk = kMode == kGemm1 ? KB : 2 * KB;
+      for (int i = threadIdx.x; i < nblk * kSmallN; i += 128)
+        cp_async4(smem_u32(dst + i),
+                  p.a_scale + static_cast<int64_t>(i >> 4) * p.npad + cu.row0 + (i & 15));
+      if constexpr (kMode == kGemm1) {
+        // W1 scale [E, 2I/128, H/128]: X1 block n, X2 block I/128 + n.
+        const int ib = p.inter / kBlockK;
+        const float* ws_x1 = p.b_scale + (static_cast<int64_t>(cu.e) * 2 * ib + cu.n) * KB;
+        for (int i = threadIdx.x; i < 2 * KB; i += 128)
+          cp_async4(smem_u32(dst_w + i), ws_x1 + (i < KB ? i : static_cast<int64_t>(ib) * KB + i - KB));
+      } else {
+        // W2 scale [E, H/128, I/128].
+        const float* ws = p.b_scale + (static_cast<int64_t>(cu.e) * (p.hidden / kBlockK) + cu.n) * KB;
+        for (int i = threadIdx.x; i < KB; i += 128) cp_async4(smem_u32(dst_w + i), ws + i);
+      }
+      cp_async_commit();
+    };
+    if (static_cast<int>(blockIdx.x) < total_units)
+      stage_scales(decode_small(blockIdx.x, ustart_s, counts_s, tstart_s, E, NT), scale_s);
     for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
       const SmallUnit c = decode_small(u, ustart_s, counts_s, tstart_s, E, NT);
       constexpr int kAcc = kMode == kGemm1 ? 2 * kSmallN : kSmallN;
       float acc[kAcc];
 #pragma unroll
       for (int i = 0; i < kAcc; ++i) acc[i] = 0.f;
-      // Stage the unit's scales: one round of loads per unit instead of a
-      // dependent global load per K block.  The copy used alternates with the
-      // unit parity; the barrier below also guarantees that no warp still reads
-      // the copy the next-but-one unit overwrites.
+      // The unit's scales were staged in shared memory by 4-byte cp.async
+      // copies issued during the previous unit (one DRAM round trip per unit,
+      // hidden behind that unit's work); wait for this thread's copies, then for
+      // every warp's.
       float* sc = scale_s + (unit_parity & 1u) * kSmallScaleFloats;
       float* sc_w = sc + kSmallMaxBlk * kSmallN;
       ++unit_parity;
-      {
-        const int nblk = kMode == kGemm1 ? KB : 2 * KB;
-        for (int i = threadIdx.x; i < nblk * kSmallN; i += 128)
-          sc[i] = __ldg(p.a_scale + static_cast<int64_t>(i >> 4) * p.npad + c.row0 + (i & 15));
-        if constexpr (kMode == kGemm1) {
-          // W1 scale [E, 2I/128, H/128]: X1 block n, X2 block I/128 + n.
-          const int ib = p.inter / kBlockK;
-          const float* ws_x1 = p.b_scale + (static_cast<int64_t>(c.e) * 2 * ib + c.n) * KB;
-          for (int i = threadIdx.x; i < 2 * KB; i += 128)
-            sc_w[i] = __ldg(ws_x1 + (i < KB ? i : static_cast<int64_t>(ib) * KB + i - KB));
-        } else {
-          // W2 scale [E, H/128, I/128].
-          const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * (p.hidden / kBlockK) + c.n) * KB;
-          for (int i = threadIdx.x; i < KB; i += 128) sc_w[i] = __ldg(ws + i);
-        }
-        if (!epi_sync(ebar, ephase, lane, abort_flag, p.ctrl)) goto epi_done;
-      }
+      cp_async_wait_all();
+      if (!epi_sync(ebar, ephase, lane, abort_flag, p.ctrl)) goto epi_done;
+      // All warps are past the previous unit: its copy can take the next unit's.
+      if (u + static_cast<int>(gridDim.x) < total_units)
+        stage_scales(decode_small(u + gridDim.x, ustart_s, counts_s, tstart_s, E, NT),
+                     scale_s + (unit_parity & 1u) * kSmallScaleFloats);
       if constexpr (kMode == kGemm1) {
         // Groups are consumed kBatch1 at a time: all their TMEM loads go out
         // before one tcgen05.wait::ld, so a batch costs one TMEM round trip.
@@ -320,16 +335,16 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
 #pragma unroll
           for (int bi = 0; bi < kBatch1; ++bi) {
             const uint32_t gg = g + bi;
-            bufs[bi] = gg % kSmallBufs;
+            bufs[bi] = gg % Cfg::kBufs;
             if (kb0 + bi < KB &&
-                !mbar_wait(&tfull[bufs[bi]], (gg / kSmallBufs) & 1u, abort_flag, p.ctrl, 14))
+                !mbar_wait(&tfull[bufs[bi]], (gg / Cfg::kBufs) & 1u, abort_flag, p.ctrl, 14))
               goto epi_done;
           }
           tc_fence_after();
           float v[kBatch1][32];
 #pragma unroll
           for (int bi = 0; bi < kBatch1; ++bi)
-            if (kb0 + bi < KB) tmem_ld32(t_lane + bufs[bi] * kSmallBufCols, v[bi]);
+            if (kb0 + bi < KB) tmem_ld32(t_lane + bufs[bi] * Cfg::kBufCols, v[bi]);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
@@ -396,16 +411,16 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
 #pragma unroll
           for (int bi = 0; bi < kBatch2; ++bi) {
             const uint32_t gg = g + bi;
-            bufs[bi] = gg % kSmallBufs;
+            bufs[bi] = gg % Cfg::kBufs;
             if (g0 + bi < ngroups &&
-                !mbar_wait(&tfull[bufs[bi]], (gg / kSmallBufs) & 1u, abort_flag, p.ctrl, 15))
+                !mbar_wait(&tfull[bufs[bi]], (gg / Cfg::kBufs) & 1u, abort_flag, p.ctrl, 15))
               goto epi_done;
           }
           tc_fence_after();
           float v[kBatch2][kSmallN];
 #pragma unroll
           for (int bi = 0; bi < kBatch2; ++bi)
-            if (g0 + bi < ngroups) tmem_ld16(t_lane + bufs[bi] * kSmallBufCols, v[bi]);
+            if (g0 + bi < ngroups) tmem_ld16(t_lane + bufs[bi] * Cfg::kBufCols, v[bi]);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
@@ -444,7 +459,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         }
       }
     }
-  epi_done:;
+  epi_done:
+    cp_async_wait_all();   // scale copies still in flight after an abort
   }
 
   tc_fence_before();
