@@ -176,6 +176,23 @@ def test_layer_graph_replay(cuda_device, t):
         assert (out_g.float() - out_e.float()).abs().max().item() <= 2e-3
 
 
+@pytest.mark.parametrize("t", [5, 700])
+def test_odd_layer_shape(cuda_device, t):
+    """H=1024, I=384 (three 128-feature tiles, odd), 64 experts in 8 groups of 8,
+    top-2 groups / top-6: both GEMM paths (t=5 decode-sized, t=700 prefill) against
+    the oracle."""
+    shape = workloads.MoeShape(t=t, hidden=1024, inter=384, e_global=64, e_local=64, n_group=8,
+                               topk_group=2, top_k=6)
+    inp = workloads.make_inputs(shape, seed=300 + t, device="cuda")
+    out, views, _ = run_cuda(inp, shape)
+    check_routing_and_dispatch(views, inp, shape)
+    toks = np.arange(t) if t <= 16 else np.random.default_rng(t).choice(t, 24, replace=False)
+    ref = oracle_output(inp, shape, tokens=toks)
+    got = bf16_np(out)[toks]
+    assert mo.cosine(got, ref) >= COS
+    np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
+
+
 def test_zero_tokens_is_a_noop(cuda_device):
     inp, shape = dsv3_inputs(0, seed=1, e_local=32)
     out, _, _ = run_cuda(inp, shape)
