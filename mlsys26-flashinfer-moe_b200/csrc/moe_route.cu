@@ -234,30 +234,56 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
   __syncthreads();
   const int n_assign = (t1 - t0) * p.top_k;
   const int hb = p.H / kBlockK;
+  // Scales: one thread per assignment, loads issued in batches of 8 before
+  // their stores (restrict-qualified: the compiler may not otherwise overlap a
+  // load with the previous store).
+  const float* __restrict__ hs = p.hs_scale;
+  float* __restrict__ asp = p.a_scale_perm;
   for (int j = tid; j < n_assign; j += kRouteThreads) {
     const int row = rows_s[j];
     if (row < 0) continue;
     const int t = t0 + j / p.top_k;
     p.row_token[row] = t;
     p.row_weight[row] = p.topk_weights[static_cast<int64_t>(t) * p.top_k + j % p.top_k];
-    for (int kb = 0; kb < hb; ++kb)
-      p.a_scale_perm[static_cast<int64_t>(kb) * p.npad + row] =
-          __ldg(p.hs_scale + static_cast<int64_t>(kb) * p.scale_ld + t);
+    for (int kb0 = 0; kb0 < hb; kb0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (kb0 + i < hb) v[i] = __ldg(hs + static_cast<int64_t>(kb0 + i) * p.scale_ld + t);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (kb0 + i < hb) asp[static_cast<int64_t>(kb0 + i) * p.npad + row] = v[i];
+    }
   }
   if (p.zero_rows) {
     const int64_t n4 = static_cast<int64_t>(t1 - t0) * p.H / 4;
     float4* z = reinterpret_cast<float4*>(p.zero_rows + static_cast<int64_t>(t0) * p.H);
     for (int64_t i = tid; i < n4; i += kRouteThreads) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  // FP8 rows: one warp per assignment, 16-byte vectors.
+  // FP8 rows: one warp per assignment, 16-byte vectors, each lane's loads of a
+  // row issued before its stores.
   const int vec = p.H / 16;
+  const uint8_t* __restrict__ hid = p.hidden;
+  uint8_t* __restrict__ ap = p.a_perm;
   for (int j = warp; j < n_assign; j += kRouteThreads / 32) {
     const int row = rows_s[j];
     if (row < 0) continue;
     const int t = t0 + j / p.top_k;
-    const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(t) * p.H);
-    uint4* dst = reinterpret_cast<uint4*>(p.a_perm + static_cast<int64_t>(row) * p.H);
-    for (int c = lane; c < vec; c += 32) dst[c] = __ldg(src + c);
+    const uint4* src = reinterpret_cast<const uint4*>(hid + static_cast<int64_t>(t) * p.H);
+    uint4* dst = reinterpret_cast<uint4*>(ap + static_cast<int64_t>(row) * p.H);
+    for (int c0 = 0; c0 < vec; c0 += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + 32 * i + lane;
+        if (c < vec) v[i] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + 32 * i + lane;
+        if (c < vec) dst[c] = v[i];
+      }
+    }
   }
 }
 
