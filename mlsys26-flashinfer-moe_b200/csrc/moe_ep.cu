@@ -156,9 +156,19 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(DispatchParams 
       if (lane == 0) report_error(p.ctrl, MOE_ERR_INVALID_ARG, 1000 + d);
       continue;
     }
-    const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(t) * p.H);
-    uint4* dst = reinterpret_cast<uint4*>(p.peers.recv_x[d] + slot * p.H);
-    for (int c = lane; c < vec; c += 32) dst[c] = __ldg(src + c);
+    const uint4* __restrict__ src =
+        reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(t) * p.H);
+    uint4* __restrict__ dst = reinterpret_cast<uint4*>(p.peers.recv_x[d] + slot * p.H);
+    // loads of a row batched ahead of their stores
+    for (int c0 = 0; c0 < vec; c0 += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (c0 + 32 * i + lane < vec) v[i] = __ldg(src + c0 + 32 * i + lane);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (c0 + 32 * i + lane < vec) dst[c0 + 32 * i + lane] = v[i];
+    }
     const float4* ls = reinterpret_cast<const float4*>(p.logits + static_cast<int64_t>(t) * p.E);
     float4* ld = reinterpret_cast<float4*>(p.peers.recv_logits[d] + slot * p.E);
     for (int c = lane; c < lvec; c += 32) ld[c] = __ldg(ls + c);
@@ -200,14 +210,31 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(CombineParams p)
       if (lane == 0) report_error(p.ctrl, MOE_ERR_INVALID_ARG, 2000 + s);
       continue;
     }
-    const float4* src = reinterpret_cast<const float4*>(p.out_f32 + static_cast<int64_t>(r) * p.H);
-    uint4* dst = reinterpret_cast<uint4*>(
+    const float4* __restrict__ src =
+        reinterpret_cast<const float4*>(p.out_f32 + static_cast<int64_t>(r) * p.H);
+    uint4* __restrict__ dst = reinterpret_cast<uint4*>(
         p.peers.comb[s] + (static_cast<int64_t>(p.rank) * p.T_max + t) * p.H);
-    for (int c = lane; c < v8; c += 32) {
-      const float4 a = __ldcs(src + 2 * c), b = __ldcs(src + 2 * c + 1);
-      __nv_bfloat162 h[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
-                             __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
-      dst[c] = *reinterpret_cast<uint4*>(h);
+    for (int c0 = 0; c0 < v8; c0 += 32 * 4) {
+      float4 a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = c0 + 32 * i + lane;
+        if (c < v8) {
+          a[i] = __ldcs(src + 2 * c);
+          b[i] = __ldcs(src + 2 * c + 1);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = c0 + 32 * i + lane;
+        if (c < v8) {
+          __nv_bfloat162 h[4] = {__floats2bfloat162_rn(a[i].x, a[i].y),
+                                 __floats2bfloat162_rn(a[i].z, a[i].w),
+                                 __floats2bfloat162_rn(b[i].x, b[i].y),
+                                 __floats2bfloat162_rn(b[i].z, b[i].w)};
+          dst[c] = *reinterpret_cast<uint4*>(h);
+        }
+      }
     }
   }
   __threadfence_system();
