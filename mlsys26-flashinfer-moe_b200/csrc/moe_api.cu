@@ -388,8 +388,6 @@ int num_sms(int* out) {
   return MOE_OK;
 }
 
-size_t workspace_bytes_for(const MoeFwdArgs* a) { return make_layout(a).w.total_bytes; }
-
 MoeWorkspaceLayout workspace_layout_for(const MoeFwdArgs* a) { return make_layout(a).w; }
 
 }  // namespace moe

@@ -34,7 +34,6 @@
 // the handle's error word instead of writing.
 #include "moe_kernels.cuh"
 
-#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -368,8 +367,7 @@ int moe_ep_create(const MoeEpConfig* cfg, MoeEp** out) {
     return MOE_ERR_CUDA;
   }
   // shapes are checked by the single-GPU validator on the receive-side args
-  MoeFwdArgs ra = recv_args(ep);
-  ra.routing_logits = reinterpret_cast<const float*>(1);
+  const MoeFwdArgs ra = recv_args(ep);
   if (int st = validate_shape_public(&ra)) {
     delete ep;
     return st;

@@ -118,7 +118,6 @@ int launch_gemm_small(int mode, const CUtensorMap& tm_w, const CUtensorMap& tm_t
 // GEMM2 into the workspace's out_f32; no memset of the whole accumulator and no
 // bf16 finalize.  Used by the expert-parallel receive side (moe_ep.cu).
 int forward_device_rows(const MoeFwdArgs* a, const int* T_dev, cudaStream_t s);
-size_t workspace_bytes_for(const MoeFwdArgs* a);
 int validate_shape_public(const MoeFwdArgs* a);
 // Router + expert histogram only, into a->workspace (layout of a full forward).
 int route_only(const MoeFwdArgs* a, cudaStream_t s);

@@ -24,8 +24,8 @@ mantissa carry corrupt the exponent (``triton/runtime/interpreter.py``
 even conversion, which is what the compiled GPU kernel does; everything else in
 the interpreter is left as is.
 
-Usage: ``python tests/golden/make_golden.py [--ref DIR]`` (needs the reference
-checkout; the committed .npz files are what the tests read).
+Usage: ``python tests/golden/make_golden.py --ref DIR`` (DIR: a checkout of the
+reference; the committed .npz files are what the tests read).
 """
 from __future__ import annotations
 
@@ -167,7 +167,7 @@ def make_case(ref, name: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference solution (read-only)")
     ap.add_argument("--case", default=None)
     a = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
