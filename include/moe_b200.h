@@ -65,7 +65,7 @@ typedef struct MoeFwdArgs {
   const void* gemm2_weights;
   const float* gemm2_weights_scale;
   void* output;
-  int64_t T;                   /* tokens (may be 0) */
+  int64_t T;                   /* tokens (may be 0), at most 2^24 */
   int64_t H;                   /* hidden size, multiple of 256 */
   int64_t I;                   /* intermediate size, multiple of 128 */
   int64_t E_global;            /* routed experts, <= 256 */

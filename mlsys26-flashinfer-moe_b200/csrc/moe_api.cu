@@ -21,7 +21,9 @@ bool is_pow2(int64_t x) { return x > 0 && (x & (x - 1)) == 0; }
 // Shape rules, mirroring the reference's asserts (kernel.py:591-607) but
 // generalised to any layer this kernel family supports.
 int validate_shape(const MoeFwdArgs* a) {
-  if (a->T < 0 || a->T > (int64_t(1) << 28)) return MOE_ERR_SHAPE;
+  // Row numbers of the expert-padded buffers (up to T * top_k + E * 127) are
+  // 32-bit: T <= 2^24 keeps them far from overflow.
+  if (a->T < 0 || a->T > (int64_t(1) << 24)) return MOE_ERR_SHAPE;
   if (a->H < 256 || a->H % 256 != 0 || a->H > 65536) return MOE_ERR_SHAPE;
   if (a->I < 128 || a->I % 128 != 0 || a->I > 65536) return MOE_ERR_SHAPE;
   const int64_t e = a->E_global;

@@ -97,7 +97,8 @@ def test_workspace_layout_is_consistent():
 @pytest.mark.parametrize("bad", [
     dict(H=7000), dict(I=100), dict(E_global=300), dict(n_group=7), dict(top_k=9),
     dict(topk_group=9), dict(E_local=0), dict(local_expert_offset=250, E_local=32),
-    dict(T=-1), dict(top_k=8, topk_group=1, n_group=64), dict(E_global=48, E_local=48, n_group=4)])
+    dict(T=-1), dict(T=(1 << 24) + 1), dict(top_k=8, topk_group=1, n_group=64),
+    dict(E_global=48, E_local=48, n_group=4)])
 def test_invalid_shapes_are_rejected(bad):
     st, _ = _ws(_args(**bad))
     assert st == _lib.MOE_ERR_SHAPE
