@@ -49,6 +49,14 @@ struct Layout {
   int blocks;
 };
 
+// Decode-shaped batches (few rows per expert on average) take the
+// swapped-operand kernels; the choice only depends on the shape, never on the
+// routing, and both paths are exact for any routing.
+bool use_small_path(const MoeFwdArgs* a) {
+  return a->T * a->top_k <= kSmallPathMaxAvgRows * a->E_global &&
+         a->H / kBlockK <= kSmallMaxScaleBlocks && a->I / 64 <= kSmallMaxScaleBlocks;
+}
+
 Layout make_layout(const MoeFwdArgs* a) {
   Layout L{};
   const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local, K = a->top_k;
@@ -214,8 +222,7 @@ T* ws_ptr(const MoeFwdArgs* a, size_t off) {
   return reinterpret_cast<T*>(static_cast<uint8_t*>(a->workspace) + off);
 }
 
-int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
-                 const int* T_dev = nullptr) {
+RouteParams route_params(const MoeFwdArgs* a, const Layout& L, const int* T_dev) {
   const MoeWorkspaceLayout& w = L.w;
   RouteParams rp{};
   rp.logits = a->routing_logits;
@@ -240,6 +247,12 @@ int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   rp.tile_start = ws_ptr<int>(a, w.tile_start);
   rp.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
   rp.T_dev = T_dev;
+  return rp;
+}
+
+int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
+                 const int* T_dev = nullptr) {
+  const RouteParams rp = route_params(a, L, T_dev);
   if (cudaMemsetAsync(rp.ctrl, 0, sizeof(CtrlBlock), s) != cudaSuccess) return MOE_ERR_CUDA;
   moe_route_kernel<<<L.blocks, kRouteThreads, 0, s>>>(rp);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
@@ -263,12 +276,6 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   const MoeWorkspaceLayout& w = L.w;
   const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local;
   float* out_f32 = ws_ptr<float>(a, w.out_f32);
-  if (!T_dev && cudaMemsetAsync(out_f32, 0, sizeof(float) * T * H, s) != cudaSuccess)
-    return MOE_ERR_CUDA;
-  st = launch_route(a, L, s, T_dev);
-  if (st) return st;
-  if ((st = record(ev, 1, s))) return st;
-
   PermuteParams pp{};
   pp.T = static_cast<int>(T);
   pp.H = static_cast<int>(H);
@@ -290,15 +297,36 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   pp.row_weight = ws_ptr<float>(a, w.row_weight);
   pp.a_perm = ws_ptr<uint8_t>(a, w.a_perm);
   pp.a_scale_perm = ws_ptr<float>(a, w.a_scale_perm);
-  moe_permute_kernel<<<L.blocks, kRouteThreads, 0, s>>>(pp);
-  if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
-  if ((st = record(ev, 2, s))) return st;
 
-  // Decode-shaped batches (few rows per expert on average) take the
-  // swapped-operand kernels; the choice only depends on the shape, never on
-  // the routing, and both paths are exact for any routing.
-  const bool small = a->T * a->top_k <= kSmallPathMaxAvgRows * a->E_global &&
-                     H / kBlockK <= kSmallMaxScaleBlocks && I / 64 <= kSmallMaxScaleBlocks;
+  if (!T_dev && T <= kTinyMaxTokens) {
+    // Decode-sized batch: one launch routes, schedules and packs (block 0)
+    // and zeroes the accumulator (the other blocks); events[1] and [2] mark
+    // its end.
+    RouteParams rp = route_params(a, L, nullptr);
+    rp.tokens_per_block = static_cast<int>(T);
+    const int64_t n4 = T * H / 4;
+    int64_t zblocks = (n4 + 4 * kRouteThreads - 1) / (4 * kRouteThreads);
+    if (zblocks < 1) zblocks = 1;
+    if (zblocks > 32) zblocks = 32;
+    moe_route_permute_tiny_kernel<<<static_cast<int>(1 + zblocks), kRouteThreads, 0, s>>>(
+        rp, pp, out_f32, n4);
+    if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+    if ((st = record(ev, 1, s))) return st;
+    if ((st = record(ev, 2, s))) return st;
+  } else {
+    if (!T_dev && cudaMemsetAsync(out_f32, 0, sizeof(float) * T * H, s) != cudaSuccess)
+      return MOE_ERR_CUDA;
+    st = launch_route(a, L, s, T_dev);
+    if (st) return st;
+    if ((st = record(ev, 1, s))) return st;
+    if (launch_programmatic(moe_permute_kernel, dim3(L.blocks), dim3(kRouteThreads), 0, s, pp) !=
+        cudaSuccess)
+      return MOE_ERR_CUDA;
+    if ((st = record(ev, 2, s))) return st;
+  }
+
+  const bool small = use_small_path(a);
+
   const uint32_t tok_box = small ? 16u : static_cast<uint32_t>(kTileM);
   CUtensorMap tm_a1, tm_b1, tm_a2, tm_b2;
   if ((st = byte_tile_map(pp.a_perm, H, w.npad, &tm_a1, tok_box))) return st;
@@ -351,8 +379,10 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   const int64_t n8 = T * H / 8;
   int blocks = static_cast<int>((n8 + 255) / 256);
   if (blocks > dev->sms * 8) blocks = dev->sms * 8;
-  moe_finalize_kernel<<<blocks, 256, 0, s>>>(out_f32, static_cast<__nv_bfloat16*>(a->output), n8);
-  if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+  if (launch_programmatic(moe_finalize_kernel, dim3(blocks), dim3(256), 0, s,
+                          static_cast<const float*>(out_f32), static_cast<__nv_bfloat16*>(a->output),
+                          n8) != cudaSuccess)
+    return MOE_ERR_CUDA;
   return record(ev, 5, s);
 }
 

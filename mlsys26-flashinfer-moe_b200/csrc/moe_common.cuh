@@ -5,6 +5,7 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp8.h>
@@ -40,6 +41,43 @@ __device__ __forceinline__ unsigned long long globaltimer() {
 
 __device__ __forceinline__ void report_error(CtrlBlock* ctrl, int code, int info) {
   if (atomicCAS(&ctrl->error, 0, code) == 0) ctrl->error_info = info;
+}
+
+// ---------------------------------------------------------------------------
+// programmatic dependent launch
+// ---------------------------------------------------------------------------
+
+// Lets the next kernel in the stream (launched with programmatic stream
+// serialization) start its prologue once every CTA of this grid has issued
+// this or exited.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launches `kern` so that it may start while the previous kernel in the
+// stream finishes (programmatic stream serialization): it must call
+// griddep_wait() before reading anything that kernel writes.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_programmatic(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem,
+                                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// Waits until the previous kernel in the stream has completed and its memory
+// operations are visible; returns at once when this grid was launched without
+// programmatic serialization.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------

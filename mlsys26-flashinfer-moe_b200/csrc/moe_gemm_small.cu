@@ -33,25 +33,26 @@ namespace {
 
 constexpr int kSmallN = 16;                // token rows per unit (MMA N)
 constexpr int kSmallThreads = 192;
-constexpr int kSmallTmemCols = 256;
-constexpr int kSmallBufsMax = 16;          // TMEM accumulator groups (barrier slots)
+constexpr int kSmallTmemCols = 512;        // all of TMEM: one CTA per SM
+constexpr int kSmallBufsMax = 32;          // TMEM accumulator groups (barrier slots)
 constexpr int kTokBytes = kSmallN * kBlockK;   // 2 KB token box per K block
 // Scale blocks per unit staged in shared memory: activation / intermediate
 // scale blocks (H/128 for GEMM1, I/64 for GEMM2) x 16 token rows, and the
 // weight scales (2 x H/128 for GEMM1, I/128 for GEMM2).  Two copies, by unit
 // parity.
 constexpr int kSmallMaxBlk = static_cast<int>(kSmallMaxScaleBlocks);
-constexpr int kSmallScaleFloats = kSmallMaxBlk * kSmallN + 2 * kSmallMaxBlk;
+constexpr int kSmallSwOff = kSmallMaxBlk * kSmallN;
+constexpr int kSmallRowOff = kSmallSwOff + 2 * kSmallMaxBlk;   // GEMM2: token, weight of the 16 rows
+constexpr int kSmallScaleFloats = kSmallRowOff + 2 * kSmallN;
 
 template <int kMode>
 struct SmallCfg {
   static constexpr int kWBytes = kMode == kGemm1 ? 2 * kTileM * kBlockK : kTileM * kBlockK;
   static constexpr int kStageBytes = kWBytes + kTokBytes;
   static constexpr int kStages = kMode == kGemm1 ? 6 : 11;
-  static constexpr int kGroups = kMode == kGemm1 ? 1 : 2;   // scale groups per K block
   // TMEM groups in the 256 allocated columns: GEMM1 groups hold the X1 and X2
   // chains (2 x 16 columns), GEMM2 groups 16 columns.
-  static constexpr int kBufCols = kMode == kGemm1 ? 2 * kSmallN : kSmallN;
+  static constexpr int kBufCols = 2 * kSmallN;
   static constexpr int kBufs = kSmallTmemCols / kBufCols;
 };
 
@@ -82,6 +83,59 @@ __device__ __forceinline__ SmallUnit decode_small(int u, const int* ustart, cons
   c.row0 = tstart[lo] * kTileM + t * kSmallN;
   c.nrows = min(kSmallN, counts[lo] - t * kSmallN);
   return c;
+}
+
+// A CTA's work as segments (unit, K blocks [kb0, kb1)).  Units are whole and
+// dealt round-robin, except in GEMM2 when there are few of them (`split`:
+// fewer than kSplitUnitsPerCta per CTA, where a partial last wave would leave
+// SMs idle): then the flattened (unit, K block) space is cut into one
+// contiguous range per CTA, so every CTA streams the same number of weight
+// tiles, and the pieces of a unit cut between CTAs each add their partial
+// product to the output (exact with the epilogue's fp32 reductions).  GEMM1
+// is never split: its SwiGLU needs whole sums, and measured at one token the
+// fix-up of split units cost more than the idle SMs.
+constexpr int kSplitUnitsPerCta = 8;
+
+struct Seg {
+  int u, kb0, kb1;   // u < 0: no more work
+};
+
+struct SegSpace {
+  bool split;
+  int total_units, KB;
+  int64_t n_items;   // total_units * KB
+  int ctas;          // CTAs with work in split mode: min(grid, n_items), each range non-empty
+  __device__ __forceinline__ int64_t lo(int b) const { return static_cast<int64_t>(b) * n_items / ctas; }
+  __device__ __forceinline__ Seg first() const {
+    const int b = blockIdx.x;
+    if (!split) return b < total_units ? Seg{b, 0, KB} : Seg{-1, 0, 0};
+    if (b >= ctas) return Seg{-1, 0, 0};
+    const int64_t a = lo(b), e = lo(b + 1);
+    const int u = static_cast<int>(a / KB);
+    const int kb0 = static_cast<int>(a - static_cast<int64_t>(u) * KB);
+    return Seg{u, kb0, static_cast<int>(min(static_cast<int64_t>(KB), kb0 + e - a))};
+  }
+  __device__ __forceinline__ Seg next(const Seg& sg) const {
+    if (!split) {
+      const int u = sg.u + static_cast<int>(gridDim.x);
+      return u < total_units ? Seg{u, 0, KB} : Seg{-1, 0, 0};
+    }
+    const int64_t it = static_cast<int64_t>(sg.u) * KB + sg.kb1;
+    const int64_t e = lo(static_cast<int>(blockIdx.x) + 1);
+    if (it >= e) return Seg{-1, 0, 0};
+    return Seg{sg.u + 1, 0, static_cast<int>(min(static_cast<int64_t>(KB), e - it))};
+  }
+};
+
+__device__ __forceinline__ SegSpace make_seg_space(int total_units, int KB, bool may_split) {
+  SegSpace sp;
+  sp.total_units = total_units;
+  sp.KB = KB;
+  sp.n_items = static_cast<int64_t>(total_units) * KB;
+  sp.split = may_split && total_units > 0 &&
+             total_units < kSplitUnitsPerCta * static_cast<int>(gridDim.x);
+  sp.ctas = static_cast<int>(min(static_cast<int64_t>(gridDim.x), sp.n_items));
+  return sp;
 }
 
 __device__ __forceinline__ void drain_wait_s(uint64_t* bar, uint32_t parity) {
@@ -132,6 +186,33 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.E_local, NT = p.n_tiles, KB = p.num_k_blocks;
 
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < Cfg::kBufs; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
+    mbar_init(ebar, 4);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, kSmallTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_tok);
+  }
+  // Everything above only touches this CTA's own resources; the routing
+  // tables and every later read come from the kernels before this one, which
+  // (under programmatic dependent launch) may still be finishing.
+  griddep_launch_dependents();
+  griddep_wait();
   for (int i = threadIdx.x; i < E; i += kSmallThreads) {
     counts_s[i] = p.counts[i];
     tstart_s[i] = p.tile_start[i];
@@ -163,33 +244,12 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     }
     if (lane == 31 && E == kMaxExperts) ustart_s[E] = incl;
   }
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < Cfg::kBufs; ++b) {
-      mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
-    }
-    mbar_init(drain, 1);
-    mbar_init(ebar, 4);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, kSmallTmemCols);
-    tmem_relinquish();
-  }
-  if (warp == 4 && lane == 0) {
-    tma_prefetch_desc(&tm_w);
-    tma_prefetch_desc(&tm_tok);
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_units = ustart_s[E];
+  const SegSpace segs = make_seg_space(total_units, KB, kMode == kGemm2);
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
@@ -197,10 +257,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0, issued_phase = 0;
-      for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-        const SmallUnit c = decode_small(u, ustart_s, counts_s, tstart_s, E, NT);
+      for (Seg sg = segs.first(); sg.u >= 0; sg = segs.next(sg)) {
+        const SmallUnit c = decode_small(sg.u, ustart_s, counts_s, tstart_s, E, NT);
         const int w_row0 = c.e * p.b_rows_per_expert + c.n * kTileM;
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 11)) goto producer_done;
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
           uint8_t* w_dst = sW + stage * Cfg::kWBytes;
@@ -232,16 +292,17 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t g = 0;
-      for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-        for (int kb = 0; kb < KB; ++kb) {
+      for (Seg sg = segs.first(); sg.u >= 0; sg = segs.next(sg)) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.ctrl, 12)) goto mma_done;
           tc_fence_after();
           const uint64_t wd = w_desc0 + ((static_cast<uint32_t>(stage) * Cfg::kWBytes) >> 4);
           const uint64_t td = t_desc0 + ((static_cast<uint32_t>(stage) * kTokBytes) >> 4);
-#pragma unroll
-          for (int gi = 0; gi < Cfg::kGroups; ++gi, ++g) {
+          {
             const uint32_t buf = g % Cfg::kBufs;
-            if (!mbar_wait(&tempty[buf], ((g / Cfg::kBufs) & 1u) ^ 1u, abort_flag, p.ctrl, 13))
+            const uint32_t free_parity = ((g / Cfg::kBufs) & 1u) ^ 1u;
+            ++g;
+            if (!mbar_wait(&tempty[buf], free_parity, abort_flag, p.ctrl, 13))
               goto mma_done;
             tc_fence_after();
             const uint32_t d = tmem_base + buf * Cfg::kBufCols;
@@ -256,13 +317,18 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
               umma_f8_group<4>(d, a, b, idesc);
               umma_f8_group<4>(d + kSmallN, a2, b, idesc);
             } else {
-              uint64_t a[2], b[2];
+              // the two 64-deep halves (one intermediate scale block each)
+              // into the two 16-column halves of the group
+              uint64_t a[2], b[2], a2[2], b2[2];
 #pragma unroll
               for (int kk = 0; kk < 2; ++kk) {
-                a[kk] = wd + (((gi * 2 + kk) * 32) >> 4);
-                b[kk] = td + (((gi * 2 + kk) * 32) >> 4);
+                a[kk] = wd + ((kk * 32) >> 4);
+                b[kk] = td + ((kk * 32) >> 4);
+                a2[kk] = wd + ((64 + kk * 32) >> 4);
+                b2[kk] = td + ((64 + kk * 32) >> 4);
               }
               umma_f8_group<2>(d, a, b, idesc);
+              umma_f8_group<2>(d + kSmallN, a2, b2, idesc);
             }
             umma_commit(&tfull[buf]);
           }
@@ -287,7 +353,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     // Copies the scales of unit cu into dst: activation / intermediate scale
     // blocks x 16 rows, then the weight scales.
     auto stage_scales = [&](const SmallUnit& cu, float* dst) {
-      float* dst_w = dst + kSmallMaxBlk * kSmallN;
+      float* dst_w = dst + kSmallSwOff;
       const int nblk = kMode == kGemm1 ? KB : 2 * KB;
       for (int i = threadIdx.x; i < nblk * kSmallN; i += 128)
         cp_async4(smem_u32(dst + i),
@@ -302,13 +368,21 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         // W2 scale [E, H/128, I/128].
         const float* ws = p.b_scale + (static_cast<int64_t>(cu.e) * (p.hidden / kBlockK) + cu.n) * KB;
         for (int i = threadIdx.x; i < KB; i += 128) cp_async4(smem_u32(dst_w + i), ws + i);
+        // token and routing weight of the 16 rows, read by the unit's output
+        // step (rows past the expert's count are padding and never used)
+        if (threadIdx.x < 2 * kSmallN) {
+          const int j = threadIdx.x & (kSmallN - 1);
+          const void* src = threadIdx.x < kSmallN ? static_cast<const void*>(p.row_token + cu.row0 + j)
+                                                  : static_cast<const void*>(p.row_weight + cu.row0 + j);
+          cp_async4(smem_u32(dst + kSmallRowOff + threadIdx.x), src);
+        }
       }
       cp_async_commit();
     };
-    if (static_cast<int>(blockIdx.x) < total_units)
-      stage_scales(decode_small(blockIdx.x, ustart_s, counts_s, tstart_s, E, NT), scale_s);
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-      const SmallUnit c = decode_small(u, ustart_s, counts_s, tstart_s, E, NT);
+    const Seg first = segs.first();
+    if (first.u >= 0) stage_scales(decode_small(first.u, ustart_s, counts_s, tstart_s, E, NT), scale_s);
+    for (Seg sg = first; sg.u >= 0; sg = segs.next(sg)) {
+      const SmallUnit c = decode_small(sg.u, ustart_s, counts_s, tstart_s, E, NT);
       constexpr int kAcc = kMode == kGemm1 ? 2 * kSmallN : kSmallN;
       float acc[kAcc];
 #pragma unroll
@@ -318,25 +392,27 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       // hidden behind that unit's work); wait for this thread's copies, then for
       // every warp's.
       float* sc = scale_s + (unit_parity & 1u) * kSmallScaleFloats;
-      float* sc_w = sc + kSmallMaxBlk * kSmallN;
+      float* sc_w = sc + kSmallSwOff;
       ++unit_parity;
       cp_async_wait_all();
       if (!epi_sync(ebar, ephase, lane, abort_flag, p.ctrl)) goto epi_done;
       // All warps are past the previous unit: its copy can take the next unit's.
-      if (u + static_cast<int>(gridDim.x) < total_units)
-        stage_scales(decode_small(u + gridDim.x, ustart_s, counts_s, tstart_s, E, NT),
+      const Seg nx = segs.next(sg);
+      if (nx.u >= 0)
+        stage_scales(decode_small(nx.u, ustart_s, counts_s, tstart_s, E, NT),
                      scale_s + (unit_parity & 1u) * kSmallScaleFloats);
       if constexpr (kMode == kGemm1) {
         // Groups are consumed kBatch1 at a time: all their TMEM loads go out
         // before one tcgen05.wait::ld, so a batch costs one TMEM round trip.
         constexpr int kBatch1 = 2;
-        for (int kb0 = 0; kb0 < KB; kb0 += kBatch1) {
+        const int kb_end = sg.kb1;
+        for (int kb0 = sg.kb0; kb0 < kb_end; kb0 += kBatch1) {
           uint32_t bufs[kBatch1];
 #pragma unroll
           for (int bi = 0; bi < kBatch1; ++bi) {
             const uint32_t gg = g + bi;
             bufs[bi] = gg % Cfg::kBufs;
-            if (kb0 + bi < KB &&
+            if (kb0 + bi < kb_end &&
                 !mbar_wait(&tfull[bufs[bi]], (gg / Cfg::kBufs) & 1u, abort_flag, p.ctrl, 14))
               goto epi_done;
           }
@@ -344,17 +420,17 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
           float v[kBatch1][32];
 #pragma unroll
           for (int bi = 0; bi < kBatch1; ++bi)
-            if (kb0 + bi < KB) tmem_ld32(t_lane + bufs[bi] * Cfg::kBufCols, v[bi]);
+            if (kb0 + bi < kb_end) tmem_ld32(t_lane + bufs[bi] * Cfg::kBufCols, v[bi]);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
 #pragma unroll
           for (int bi = 0; bi < kBatch1; ++bi)
-            if (kb0 + bi < KB && lane == 0) mbar_arrive(&tempty[bufs[bi]]);
+            if (kb0 + bi < kb_end && lane == 0) mbar_arrive(&tempty[bufs[bi]]);
 #pragma unroll
           for (int bi = 0; bi < kBatch1; ++bi) {
             const int kb = kb0 + bi;
-            if (kb < KB) {
+            if (kb < kb_end) {
               const float w1 = sc_w[kb], w2 = sc_w[KB + kb];
               const float4* s4 = reinterpret_cast<const float4*>(sc + kb * kSmallN);
 #pragma unroll
@@ -402,44 +478,49 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         // red_s is rewritten by the next unit
         if (!epi_sync(ebar, ephase, lane, abort_flag, p.ctrl)) goto epi_done;
       } else {
-        // Scale groups (two per K block) are consumed kBatch2 at a time, as in
-        // GEMM1.
-        constexpr int kBatch2 = 4;
-        const int ngroups = 2 * KB;
-        for (int g0 = 0; g0 < ngroups; g0 += kBatch2) {
+        // One TMEM group per K block, its two 16-column halves holding the two
+        // 64-deep partial products (one intermediate scale block each);
+        // consumed kBatch2 groups at a time, as in GEMM1.
+        constexpr int kBatch2 = 2;
+        const int kb_end = sg.kb1;
+        for (int kb0 = sg.kb0; kb0 < kb_end; kb0 += kBatch2) {
           uint32_t bufs[kBatch2];
 #pragma unroll
           for (int bi = 0; bi < kBatch2; ++bi) {
             const uint32_t gg = g + bi;
             bufs[bi] = gg % Cfg::kBufs;
-            if (g0 + bi < ngroups &&
+            if (kb0 + bi < kb_end &&
                 !mbar_wait(&tfull[bufs[bi]], (gg / Cfg::kBufs) & 1u, abort_flag, p.ctrl, 15))
               goto epi_done;
           }
           tc_fence_after();
-          float v[kBatch2][kSmallN];
+          float v[kBatch2][2 * kSmallN];
 #pragma unroll
           for (int bi = 0; bi < kBatch2; ++bi)
-            if (g0 + bi < ngroups) tmem_ld16(t_lane + bufs[bi] * Cfg::kBufCols, v[bi]);
+            if (kb0 + bi < kb_end) tmem_ld32(t_lane + bufs[bi] * Cfg::kBufCols, v[bi]);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
 #pragma unroll
           for (int bi = 0; bi < kBatch2; ++bi)
-            if (g0 + bi < ngroups && lane == 0) mbar_arrive(&tempty[bufs[bi]]);
+            if (kb0 + bi < kb_end && lane == 0) mbar_arrive(&tempty[bufs[bi]]);
 #pragma unroll
           for (int bi = 0; bi < kBatch2; ++bi) {
-            const int gi = g0 + bi;
-            if (gi < ngroups) {
-              const float sw = sc_w[gi >> 1];
-              const float4* s4 = reinterpret_cast<const float4*>(sc + gi * kSmallN);
+            const int kb = kb0 + bi;
+            if (kb < kb_end) {
+              const float sw = sc_w[kb];
 #pragma unroll
-              for (int j4 = 0; j4 < 4; ++j4) {
-                const float4 f = s4[j4];
-                acc[4 * j4] = fmaf(v[bi][4 * j4], f.x * sw, acc[4 * j4]);
-                acc[4 * j4 + 1] = fmaf(v[bi][4 * j4 + 1], f.y * sw, acc[4 * j4 + 1]);
-                acc[4 * j4 + 2] = fmaf(v[bi][4 * j4 + 2], f.z * sw, acc[4 * j4 + 2]);
-                acc[4 * j4 + 3] = fmaf(v[bi][4 * j4 + 3], f.w * sw, acc[4 * j4 + 3]);
+              for (int h = 0; h < 2; ++h) {
+                const float4* s4 = reinterpret_cast<const float4*>(sc + (2 * kb + h) * kSmallN);
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                  const float4 f = s4[j4];
+                  const float* vv = v[bi] + h * kSmallN + 4 * j4;
+                  acc[4 * j4] = fmaf(vv[0], f.x * sw, acc[4 * j4]);
+                  acc[4 * j4 + 1] = fmaf(vv[1], f.y * sw, acc[4 * j4 + 1]);
+                  acc[4 * j4 + 2] = fmaf(vv[2], f.z * sw, acc[4 * j4 + 2]);
+                  acc[4 * j4 + 3] = fmaf(vv[3], f.w * sw, acc[4 * j4 + 3]);
+                }
               }
               ++g;
             }
@@ -452,8 +533,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         for (int j = 0; j < kSmallN; ++j) {
           if (j < c.nrows) {
             const int64_t row = static_cast<int64_t>(c.row0) + j;
-            const int tok = __ldg(p.row_token + row);
-            const float w = __ldg(p.row_weight + row);
+            const int tok = reinterpret_cast<const int*>(sc + kSmallRowOff)[j];
+            const float w = sc[kSmallRowOff + kSmallN + j];
             atomicAdd(p.out_f32 + static_cast<int64_t>(tok) * p.hidden + col, acc[j] * w);
           }
         }
@@ -485,13 +566,15 @@ int gemm_small_set_smem_attrs() {
 
 int launch_gemm_small(int mode, const CUtensorMap& tm_w, const CUtensorMap& tm_tok,
                       const GemmParams& p, int grid, cudaStream_t stream) {
-  if (mode == kGemm1)
-    moe_gemm_small_kernel<kGemm1><<<grid, kSmallThreads, small_smem_bytes<kGemm1>(), stream>>>(
-        tm_w, tm_tok, p);
-  else
-    moe_gemm_small_kernel<kGemm2><<<grid, kSmallThreads, small_smem_bytes<kGemm2>(), stream>>>(
-        tm_w, tm_tok, p);
-  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+  // Both kernels wait for their predecessor inside (griddep_wait) after a
+  // prologue that only touches their own shared memory and TMEM.
+  const cudaError_t e =
+      mode == kGemm1
+          ? launch_programmatic(moe_gemm_small_kernel<kGemm1>, dim3(grid), dim3(kSmallThreads),
+                                small_smem_bytes<kGemm1>(), stream, tm_w, tm_tok, p)
+          : launch_programmatic(moe_gemm_small_kernel<kGemm2>, dim3(grid), dim3(kSmallThreads),
+                                small_smem_bytes<kGemm2>(), stream, tm_w, tm_tok, p);
+  return e == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
 }  // namespace moe

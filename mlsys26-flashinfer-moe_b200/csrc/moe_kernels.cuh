@@ -10,6 +10,7 @@ constexpr int kMaxExperts = 256;       // E_global (and hence E_local) limit
 constexpr int kMaxTopK = 8;
 constexpr int kRouteThreads = 256;     // 8 warps, one token per warp at a time
 constexpr int kMaxTokensPerBlock = 256;
+constexpr int kTinyMaxTokens = 16;   // batches routed and permuted by one block (moe_route_permute_tiny_kernel)
 constexpr int kTileM = 128;            // rows (assignments) per GEMM tile
 constexpr int kTileN = 256;            // output columns per GEMM tile
 constexpr int kBlockK = 128;           // K per pipeline stage = scale block
@@ -89,6 +90,8 @@ struct GemmParams {
 
 __global__ void moe_route_kernel(RouteParams p);
 __global__ void moe_permute_kernel(PermuteParams p);
+__global__ void moe_route_permute_tiny_kernel(RouteParams rp, PermuteParams pp, float* acc,
+                                              int64_t acc_n4);
 __global__ void moe_finalize_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out,
                                     int64_t n8);
 

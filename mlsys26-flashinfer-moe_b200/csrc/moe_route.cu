@@ -13,6 +13,8 @@
 //                       inside each expert, and packs the token's FP8 row and
 //                       scales there.  Replaces _scatter_kernel (288-324) and the
 //                       index_select packing (663-665).
+//   moe_route_permute_tiny_kernel  both of the above in one launch for decode-sized
+//                       batches.
 //   moe_finalize_kernel fp32 accumulator -> bf16 output (reference kernel.py:729).
 #include "moe_kernels.cuh"
 
@@ -157,6 +159,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
   __shared__ int warp_sum[kRouteThreads / 32];
   __shared__ int is_last;
   const int tid = threadIdx.x;
+  griddep_launch_dependents();   // the permute kernel waits for this grid inside
   for (int i = tid; i < p.E_local; i += kRouteThreads) hist_s[i] = 0;
   __syncthreads();
   switch (p.experts_per_lane) {
@@ -207,31 +210,28 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
   if (tid == 0) p.ctrl->done = 0u;
 }
 
-__global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParams p) {
-  __shared__ int cursor[kMaxExperts];
-  __shared__ int rows_s[kMaxTokensPerBlock * kMaxTopK];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int b = blockIdx.x;
-  const int T = p.T_dev ? min(p.T, *p.T_dev) : p.T;
-  const int t0 = b * p.tokens_per_block;
-  const int t1 = min(T, t0 + p.tokens_per_block);
-  for (int i = tid; i < p.E_local; i += kRouteThreads)
-    cursor[i] = kTileM * p.tile_start[i] + p.block_base[static_cast<int64_t>(b) * p.E_local + i];
-  __syncthreads();
-  // Row of every assignment, tokens in order (a token's experts are distinct,
-  // so the lanes of one token never touch the same cursor).
-  if (warp == 0) {
-    for (int t = t0; t < t1; ++t) {
-      if (lane < p.top_k) {
-        const int le = p.topk_idx[static_cast<int64_t>(t) * p.top_k + lane] - p.local_expert_offset;
-        int row = -1;
-        if (le >= 0 && le < p.E_local) row = cursor[le]++;
-        rows_s[(t - t0) * p.top_k + lane] = row;
-      }
-      __syncwarp();
+namespace {
+
+// Row of every assignment of tokens [t0, t1), tokens in order inside each
+// expert (a token's experts are distinct, so the lanes of one token never touch
+// the same cursor).  Warp 0 only; cursor[e] starts at the expert's first row.
+__device__ __forceinline__ void assign_rows(const PermuteParams& p, int* cursor, int* rows_s,
+                                            int t0, int t1, int lane) {
+  for (int t = t0; t < t1; ++t) {
+    if (lane < p.top_k) {
+      const int le = p.topk_idx[static_cast<int64_t>(t) * p.top_k + lane] - p.local_expert_offset;
+      int row = -1;
+      if (le >= 0 && le < p.E_local) row = cursor[le]++;
+      rows_s[(t - t0) * p.top_k + lane] = row;
     }
+    __syncwarp();
   }
-  __syncthreads();
+}
+
+// Packs the rows of tokens [t0, t1) into the permuted buffers: token, weight
+// and scales per assignment, then the FP8 rows.  All threads of the block.
+__device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* rows_s, int t0, int t1) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_assign = (t1 - t0) * p.top_k;
   const int hb = p.H / kBlockK;
   // Scales: one thread per assignment, loads issued in batches of 8 before
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
   // load with the previous store).
   const float* __restrict__ hs = p.hs_scale;
   float* __restrict__ asp = p.a_scale_perm;
-  for (int j = tid; j < n_assign; j += kRouteThreads) {
+  for (int j = tid; j < n_assign; j += blockDim.x) {
     const int row = rows_s[j];
     if (row < 0) continue;
     const int t = t0 + j / p.top_k;
@@ -258,14 +258,15 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
   if (p.zero_rows) {
     const int64_t n4 = static_cast<int64_t>(t1 - t0) * p.H / 4;
     float4* z = reinterpret_cast<float4*>(p.zero_rows + static_cast<int64_t>(t0) * p.H);
-    for (int64_t i = tid; i < n4; i += kRouteThreads) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t i = tid; i < n4; i += blockDim.x) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   // FP8 rows: one warp per assignment, 16-byte vectors, each lane's loads of a
   // row issued before its stores.
   const int vec = p.H / 16;
+  const int nwarps = blockDim.x >> 5;
   const uint8_t* __restrict__ hid = p.hidden;
   uint8_t* __restrict__ ap = p.a_perm;
-  for (int j = warp; j < n_assign; j += kRouteThreads / 32) {
+  for (int j = warp; j < n_assign; j += nwarps) {
     const int row = rows_s[j];
     if (row < 0) continue;
     const int t = t0 + j / p.top_k;
@@ -287,9 +288,97 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
   }
 }
 
+// Exclusive scan of the experts' 128-row tile counts (one thread per local
+// expert, E_local <= kRouteThreads): writes tile_start[0..E_local] and returns
+// this thread's start.
+__device__ __forceinline__ int scan_tiles(int tiles, int* tile_start, int E_local, int* warp_sum) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int incl = tiles;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (lane == 31) warp_sum[warp] = incl;
+  __syncthreads();
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += warp_sum[w];
+  incl += before;
+  if (tid < E_local) tile_start[tid] = incl - tiles;
+  if (tid == kRouteThreads - 1) tile_start[E_local] = incl;
+  return incl - tiles;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParams p) {
+  __shared__ int cursor[kMaxExperts];
+  __shared__ int rows_s[kMaxTokensPerBlock * kMaxTopK];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.x;
+  griddep_launch_dependents();
+  griddep_wait();   // routing results of moe_route_kernel
+  const int T = p.T_dev ? min(p.T, *p.T_dev) : p.T;
+  const int t0 = b * p.tokens_per_block;
+  const int t1 = min(T, t0 + p.tokens_per_block);
+  for (int i = tid; i < p.E_local; i += kRouteThreads)
+    cursor[i] = kTileM * p.tile_start[i] + p.block_base[static_cast<int64_t>(b) * p.E_local + i];
+  __syncthreads();
+  if (warp == 0) assign_rows(p, cursor, rows_s, t0, t1, lane);
+  __syncthreads();
+  pack_rows(p, rows_s, t0, t1);
+}
+
+// Decode-sized batches (T <= kTinyMaxTokens, host row count): routing, the
+// expert histogram, the tile schedule and the permute in block 0 of ONE launch
+// (no per-block histograms, no second kernel, no memsets); blocks 1.. zero the
+// fp32 accumulator meanwhile.  Results are those of moe_route_kernel followed
+// by moe_permute_kernel.
+__global__ void __launch_bounds__(kRouteThreads)
+    moe_route_permute_tiny_kernel(RouteParams rp, PermuteParams pp, float* acc, int64_t acc_n4) {
+  griddep_launch_dependents();   // GEMM1 waits for this grid inside
+  if (blockIdx.x > 0) {
+    float4* z = reinterpret_cast<float4*>(acc);
+    const int64_t stride = static_cast<int64_t>(gridDim.x - 1) * kRouteThreads;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x - 1) * kRouteThreads + threadIdx.x; i < acc_n4;
+         i += stride)
+      z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  __shared__ int hist_s[kMaxExperts];
+  __shared__ int cursor[kMaxExperts];
+  __shared__ int warp_sum[kRouteThreads / 32];
+  __shared__ int rows_s[kTinyMaxTokens * kMaxTopK];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < rp.E_local; i += kRouteThreads) hist_s[i] = 0;
+  if (tid == 0) {
+    rp.ctrl->done = 0u;
+    rp.ctrl->error = 0;
+    rp.ctrl->error_info = 0;
+  }
+  __syncthreads();
+  switch (rp.experts_per_lane) {
+    case 1: route_block_tokens<1>(rp, hist_s); break;
+    case 2: route_block_tokens<2>(rp, hist_s); break;
+    case 4: route_block_tokens<4>(rp, hist_s); break;
+    default: route_block_tokens<8>(rp, hist_s); break;
+  }
+  __syncthreads();
+  const int count = tid < rp.E_local ? hist_s[tid] : 0;
+  if (tid < rp.E_local) rp.counts[tid] = count;
+  const int first = scan_tiles(tid < rp.E_local ? (count + kTileM - 1) / kTileM : 0, rp.tile_start,
+                               rp.E_local, warp_sum);
+  if (tid < rp.E_local) cursor[tid] = kTileM * first;
+  __syncthreads();
+  if (warp == 0) assign_rows(pp, cursor, rows_s, 0, rp.T, lane);
+  __syncthreads();
+  pack_rows(pp, rows_s, 0, rp.T);
+}
+
 __global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restrict__ in,
                                                            __nv_bfloat16* __restrict__ out,
                                                            int64_t n8) {
+  griddep_wait();   // the accumulator is complete once GEMM2 has finished
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
        i += stride) {
