@@ -367,6 +367,11 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   g2.row_token = pp.row_token;
   g2.row_weight = pp.row_weight;
   g2.out_f32 = out_f32;
+  const bool fuse_final = small && !T_dev && T <= kFuseFinalMaxTokens;
+  if (fuse_final) {
+    g2.final_out = static_cast<__nv_bfloat16*>(a->output);
+    g2.final_n8 = T * H / 8;
+  }
   if (small) {
     g2.n_tiles = static_cast<int>(H / kTileM);
     if ((st = launch_gemm_small(kGemm2, tm_b2, tm_a2, g2, dev->sms, s))) return st;
@@ -375,6 +380,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   }
   if ((st = record(ev, 4, s))) return st;
   if (T_dev) return MOE_OK;
+  if (fuse_final) return record(ev, 5, s);
 
   const int64_t n8 = T * H / 8;
   int blocks = static_cast<int>((n8 + 255) / 256);

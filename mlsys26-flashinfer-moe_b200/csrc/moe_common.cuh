@@ -21,12 +21,14 @@ namespace moe {
 
 // Control block at the start of the workspace.  `done` is the arrival counter
 // of the routing kernel's last-block scan; `error` holds the first device-side
-// error code (MOE_ERR_TIMEOUT) and `error_info` where it happened.
+// error code (MOE_ERR_TIMEOUT) and `error_info` where it happened; `gemm_done`
+// counts finished CTAs of the decode GEMM2.  Zeroed before every forward.
 struct CtrlBlock {
   unsigned int done;
   int error;
   int error_info;
-  int pad[61];
+  unsigned int gemm_done;   // decode GEMM2 CTAs finished (bf16 output by the last)
+  int pad[60];
 };
 
 // Bounded waits give up after this many nanoseconds of %globaltimer.  Normal

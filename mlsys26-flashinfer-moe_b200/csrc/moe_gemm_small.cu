@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         // One TMEM group per K block, its two 16-column halves holding the two
         // 64-deep partial products (one intermediate scale block each);
         // consumed kBatch2 groups at a time, as in GEMM1.
-        constexpr int kBatch2 = 2;
+        constexpr int kBatch2 = 4;
         const int kb_end = sg.kb1;
         for (int kb0 = sg.kb0; kb0 < kb_end; kb0 += kBatch2) {
           uint32_t bufs[kBatch2];
@@ -542,6 +542,48 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     }
   epi_done:
     cp_async_wait_all();   // scale copies still in flight after an abort
+    if constexpr (kMode == kGemm2) {
+      if (p.final_out != nullptr) {
+        // Small batches: the last CTA to get here turns the fp32 accumulator
+        // into the bf16 output (moe_finalize_kernel's work) without another
+        // launch.  Every path out of the loop above reaches these barriers.
+        volatile int* last = reinterpret_cast<volatile int*>(red_s);
+        __threadfence();   // this thread's reductions into out_f32
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 0)
+          *last = atomicAdd(&p.ctrl->gemm_done, 1u) == gridDim.x - 1 ? 1 : 0;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (*last) {
+          __threadfence();
+          const float4* in = reinterpret_cast<const float4*>(p.out_f32);
+          uint4* out = reinterpret_cast<uint4*>(p.final_out);
+          // eight 8-float chunks per thread in flight before their stores
+          for (int64_t i0 = threadIdx.x; i0 < p.final_n8; i0 += 8 * 128) {
+            float4 a[8], b[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int64_t i = i0 + k * 128;
+              if (i < p.final_n8) {
+                a[k] = __ldcg(in + 2 * i);
+                b[k] = __ldcg(in + 2 * i + 1);
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int64_t i = i0 + k * 128;
+              if (i < p.final_n8) {
+                __nv_bfloat162 r[4];
+                r[0] = __floats2bfloat162_rn(a[k].x, a[k].y);
+                r[1] = __floats2bfloat162_rn(a[k].z, a[k].w);
+                r[2] = __floats2bfloat162_rn(b[k].x, b[k].y);
+                r[3] = __floats2bfloat162_rn(b[k].z, b[k].w);
+                out[i] = *reinterpret_cast<uint4*>(r);
+              }
+            }
+          }
+        }
+      }
+    }
   }
 
   tc_fence_before();

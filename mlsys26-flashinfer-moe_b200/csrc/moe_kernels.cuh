@@ -10,7 +10,8 @@ constexpr int kMaxExperts = 256;       // E_global (and hence E_local) limit
 constexpr int kMaxTopK = 8;
 constexpr int kRouteThreads = 256;     // 8 warps, one token per warp at a time
 constexpr int kMaxTokensPerBlock = 256;
-constexpr int kTinyMaxTokens = 16;   // batches routed and permuted by one block (moe_route_permute_tiny_kernel)
+constexpr int kTinyMaxTokens = 16;
+constexpr int kFuseFinalMaxTokens = 2;   // decode GEMM2 also writes the bf16 output   // batches routed and permuted by one block (moe_route_permute_tiny_kernel)
 constexpr int kTileM = 128;            // rows (assignments) per GEMM tile
 constexpr int kTileN = 256;            // output columns per GEMM tile
 constexpr int kBlockK = 128;           // K per pipeline stage = scale block
@@ -85,6 +86,8 @@ struct GemmParams {
   const int* row_token;    // GEMM2: token of each permuted row
   const float* row_weight; // GEMM2: routing weight of each permuted row
   float* out_f32;          // GEMM2: [T, H] accumulator
+  __nv_bfloat16* final_out;  // decode GEMM2 with few tokens: bf16 output written by the last CTA
+  int64_t final_n8;        // T * H / 8
   CtrlBlock* ctrl;
 };
 

@@ -355,6 +355,7 @@ __global__ void __launch_bounds__(kRouteThreads)
     rp.ctrl->done = 0u;
     rp.ctrl->error = 0;
     rp.ctrl->error_info = 0;
+    rp.ctrl->gemm_done = 0u;
   }
   __syncthreads();
   switch (rp.experts_per_lane) {
