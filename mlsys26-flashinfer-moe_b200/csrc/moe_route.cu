@@ -39,7 +39,7 @@ __device__ __forceinline__ float sigmoid_f32(float x) {
 // G experts spans LPG = G/EPL consecutive lanes.
 template <int EPL>
 __device__ __forceinline__ void route_one_token(const RouteParams& p, int t, int lane,
-                                                const float (&bias)[EPL], int* hist_s) {
+                                                const float (&bias)[EPL], int* hist_s, int* idx_s) {
   const unsigned full = 0xffffffffu;
   const int e0 = lane * EPL;
   const bool active = e0 < p.E;
@@ -131,6 +131,7 @@ __device__ __forceinline__ void route_one_token(const RouteParams& p, int t, int
   if (lane < p.top_k) {
     const float w = __fdiv_rn(my_s, total) * p.routed_scaling_factor;
     p.topk_idx[static_cast<int64_t>(t) * p.top_k + lane] = my_idx;
+    if (idx_s) idx_s[t * p.top_k + lane] = my_idx;
     p.topk_weights[static_cast<int64_t>(t) * p.top_k + lane] = w;
     const int le = my_idx - p.local_expert_offset;
     if (le >= 0 && le < p.E_local) atomicAdd(&hist_s[le], 1);
@@ -138,7 +139,9 @@ __device__ __forceinline__ void route_one_token(const RouteParams& p, int t, int
 }
 
 template <int EPL>
-__device__ __forceinline__ void route_block_tokens(const RouteParams& p, int* hist_s) {
+// idx_s: optional copy of the routed expert ids in shared memory (one-block launches).
+__device__ __forceinline__ void route_block_tokens(const RouteParams& p, int* hist_s,
+                                                   int* idx_s = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float bias[EPL];
 #pragma unroll
@@ -149,7 +152,8 @@ __device__ __forceinline__ void route_block_tokens(const RouteParams& p, int* hi
   const int T = p.T_dev ? min(p.T, *p.T_dev) : p.T;
   const int t0 = blockIdx.x * p.tokens_per_block;
   const int t1 = min(T, t0 + p.tokens_per_block);
-  for (int t = t0 + warp; t < t1; t += kRouteThreads / 32) route_one_token<EPL>(p, t, lane, bias, hist_s);
+  for (int t = t0 + warp; t < t1; t += kRouteThreads / 32)
+    route_one_token<EPL>(p, t, lane, bias, hist_s, idx_s);
 }
 
 }  // namespace
@@ -214,12 +218,13 @@ namespace {
 
 // Row of every assignment of tokens [t0, t1), tokens in order inside each
 // expert (a token's experts are distinct, so the lanes of one token never touch
-// the same cursor).  Warp 0 only; cursor[e] starts at the expert's first row.
-__device__ __forceinline__ void assign_rows(const PermuteParams& p, int* cursor, int* rows_s,
-                                            int t0, int t1, int lane) {
+// the same cursor).  Warp 0 only; cursor[e] starts at the expert's first row;
+// idx holds the routed expert ids [T, top_k] (global memory or a block's copy).
+__device__ __forceinline__ void assign_rows(const PermuteParams& p, const int* idx, int* cursor,
+                                            int* rows_s, int t0, int t1, int lane) {
   for (int t = t0; t < t1; ++t) {
     if (lane < p.top_k) {
-      const int le = p.topk_idx[static_cast<int64_t>(t) * p.top_k + lane] - p.local_expert_offset;
+      const int le = idx[static_cast<int64_t>(t) * p.top_k + lane] - p.local_expert_offset;
       int row = -1;
       if (le >= 0 && le < p.E_local) row = cursor[le]++;
       rows_s[(t - t0) * p.top_k + lane] = row;
@@ -239,7 +244,25 @@ __device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* row
   // load with the previous store).
   const float* __restrict__ hs = p.hs_scale;
   float* __restrict__ asp = p.a_scale_perm;
-  for (int j = tid; j < n_assign; j += blockDim.x) {
+  const int nwarps = blockDim.x >> 5;
+  // Few assignments (decode batches): a warp per assignment instead, its lanes
+  // over the (at most 64) scale blocks, so that a copy is one round trip.
+  const bool few = n_assign <= 4 * nwarps && hb <= 64;
+  for (int j = warp; few && j < n_assign; j += nwarps) {
+    const int row = rows_s[j];
+    if (row < 0) continue;
+    const int t = t0 + j / p.top_k;
+    if (lane == 0) {
+      p.row_token[row] = t;
+      p.row_weight[row] = p.topk_weights[static_cast<int64_t>(t) * p.top_k + j % p.top_k];
+    }
+    float v0 = 0.f, v1 = 0.f;
+    if (lane < hb) v0 = __ldg(hs + static_cast<int64_t>(lane) * p.scale_ld + t);
+    if (lane + 32 < hb) v1 = __ldg(hs + static_cast<int64_t>(lane + 32) * p.scale_ld + t);
+    if (lane < hb) asp[static_cast<int64_t>(lane) * p.npad + row] = v0;
+    if (lane + 32 < hb) asp[static_cast<int64_t>(lane + 32) * p.npad + row] = v1;
+  }
+  for (int j = tid; !few && j < n_assign; j += blockDim.x) {
     const int row = rows_s[j];
     if (row < 0) continue;
     const int t = t0 + j / p.top_k;
@@ -263,7 +286,6 @@ __device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* row
   // FP8 rows: one warp per assignment, 16-byte vectors, each lane's loads of a
   // row issued before its stores.
   const int vec = p.H / 16;
-  const int nwarps = blockDim.x >> 5;
   const uint8_t* __restrict__ hid = p.hidden;
   uint8_t* __restrict__ ap = p.a_perm;
   for (int j = warp; j < n_assign; j += nwarps) {
@@ -324,7 +346,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
   for (int i = tid; i < p.E_local; i += kRouteThreads)
     cursor[i] = kTileM * p.tile_start[i] + p.block_base[static_cast<int64_t>(b) * p.E_local + i];
   __syncthreads();
-  if (warp == 0) assign_rows(p, cursor, rows_s, t0, t1, lane);
+  if (warp == 0) assign_rows(p, p.topk_idx, cursor, rows_s, t0, t1, lane);
   __syncthreads();
   pack_rows(p, rows_s, t0, t1);
 }
@@ -349,6 +371,7 @@ __global__ void __launch_bounds__(kRouteThreads)
   __shared__ int cursor[kMaxExperts];
   __shared__ int warp_sum[kRouteThreads / 32];
   __shared__ int rows_s[kTinyMaxTokens * kMaxTopK];
+  __shared__ int idx_s[kTinyMaxTokens * kMaxTopK];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   for (int i = tid; i < rp.E_local; i += kRouteThreads) hist_s[i] = 0;
   if (tid == 0) {
@@ -359,10 +382,10 @@ __global__ void __launch_bounds__(kRouteThreads)
   }
   __syncthreads();
   switch (rp.experts_per_lane) {
-    case 1: route_block_tokens<1>(rp, hist_s); break;
-    case 2: route_block_tokens<2>(rp, hist_s); break;
-    case 4: route_block_tokens<4>(rp, hist_s); break;
-    default: route_block_tokens<8>(rp, hist_s); break;
+    case 1: route_block_tokens<1>(rp, hist_s, idx_s); break;
+    case 2: route_block_tokens<2>(rp, hist_s, idx_s); break;
+    case 4: route_block_tokens<4>(rp, hist_s, idx_s); break;
+    default: route_block_tokens<8>(rp, hist_s, idx_s); break;
   }
   __syncthreads();
   const int count = tid < rp.E_local ? hist_s[tid] : 0;
@@ -371,7 +394,7 @@ __global__ void __launch_bounds__(kRouteThreads)
                                rp.E_local, warp_sum);
   if (tid < rp.E_local) cursor[tid] = kTileM * first;
   __syncthreads();
-  if (warp == 0) assign_rows(pp, cursor, rows_s, 0, rp.T, lane);
+  if (warp == 0) assign_rows(pp, idx_s, cursor, rows_s, 0, rp.T, lane);
   __syncthreads();
   pack_rows(pp, rows_s, 0, rp.T);
 }
