@@ -4,27 +4,32 @@
 //
 // With 128-row token tiles a decode step would spend a full promotion pass
 // (two 256-column TMEM round trips per thread) on every 128-deep K block for
-// one to eight real rows.  Here a TMEM accumulator group is 128 lanes x 16 (or
-// 2 x 16) columns, eight of them fit in the 256 allocated columns, so the
-// tensor core runs up to eight groups ahead of the promotion and the kernel
-// streams weights at the rate HBM delivers them.
+// one to eight real rows.  Here a TMEM accumulator group is 128 lanes x 32
+// columns per 128-deep K block, sixteen of them fit in the 512 allocated
+// columns (one CTA per SM), so the tensor core runs up to sixteen K blocks ahead
+// of the promotion.  The promotion's cost per group, not its latency, is what
+// bounds these kernels: a group covering less than a whole K block (16-column
+// groups per 64-deep half in GEMM2) made GEMM2 1.27x slower.
 //
 // One CTA per SM walks work units (expert, 128 output features, 16 token rows):
 //   warps 0-3  promotion + epilogue; thread (warp q, lane l) owns output feature
 //              32q + l of the unit for all 16 token columns.
 //   warp 4     TMA producer: per 128-deep K block the weight box(es) 128 x 128
-//              and the 16 x 128 token box, into a ring of kStagesS stages.
+//              and the 16 x 128 token box, into a ring of Cfg::kStages stages.
 //   warp 5     MMA issuer: tcgen05.mma kind::f8f6f4, M=128 N=16 K=32.
+// Every kernel of a forward after the first is launched with programmatic
+// stream serialisation: barrier set-up, TMEM allocation and tensor-map prefetch
+// run before griddepcontrol.wait, overlapping the previous kernel's tail.
 //
-// kGemm1 (reference moe_gemm1_kernel, kernel.py:7-151): per unit two MMA
-//   chains into the two 16-column halves of a 32-column group, X1 = rows
-//   n*128.. of W1[e] (multiplied) and X2 = rows I + n*128.. (SiLU input);
-//   epilogue C = silu(X2) * X1, amax over 64 features (two warps), scale =
+// kGemm1 (reference moe_gemm1_kernel, kernel.py:7-151): per K block two MMA
+//   chains into the two 16-column halves of the group, X1 = rows n*128.. of
+//   W1[e] (multiplied) and X2 = rows I + n*128.. (SiLU input); epilogue
+//   C = silu(X2) * X1, amax over 64 features (two warps), scale =
 //   max(amax/448, 1e-12), C * (1/scale) -> e4m3, written to the intermediate.
-// kGemm2 (reference moe_gemm2_kernel, kernel.py:153-250): W2[e] rows n*128..,
-//   two 64-deep scale groups per K block (the intermediate's 1x64 scales),
-//   epilogue out[token] += weight * D with fp32 reductions, 128 contiguous
-//   floats per token and warp.
+// kGemm2 (reference moe_gemm2_kernel, kernel.py:153-250): W2[e] rows n*128..;
+//   the two 64-deep halves of a K block (one 1x64 intermediate scale block
+//   each) go to the two 16-column halves of the group; epilogue out[token] +=
+//   weight * D with fp32 reductions, 128 contiguous floats per token and warp.
 #include "moe_kernels.cuh"
 
 namespace moe {
