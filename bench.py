@@ -403,7 +403,8 @@ def e2e_run(torch, runner, a):
 
 def decode_sweep(torch, peaks):
     """Decode latency (T=1..64, all 256 experts), L2 flushed before every step:
-    p50 of the eager forward (five launches, no per-stage events), p50 of the
+    p50 of the eager forward (three kernels at T <= 2, four up to T=16, two
+    memsets and five kernels above; no per-stage events), p50 of the
     same forward replayed as one CUDA graph (``moe_b200.LayerGraph``), and a
     per-stage breakdown from a separate run with stage events."""
     from moe_b200 import workloads, LayerGraph
