@@ -39,7 +39,7 @@ namespace {
 constexpr int kSmallN = 16;                // token rows per unit (MMA N)
 constexpr int kSmallThreads = 192;
 constexpr int kSmallTmemCols = 512;        // all of TMEM: one CTA per SM
-constexpr int kSmallBufsMax = 32;          // TMEM accumulator groups (barrier slots)
+constexpr int kSmallBufsMax = 32;          // barrier slots for TMEM accumulator groups
 constexpr int kTokBytes = kSmallN * kBlockK;   // 2 KB token box per K block
 // Scale blocks per unit staged in shared memory: activation / intermediate
 // scale blocks (H/128 for GEMM1, I/64 for GEMM2) x 16 token rows, and the
@@ -55,10 +55,11 @@ struct SmallCfg {
   static constexpr int kWBytes = kMode == kGemm1 ? 2 * kTileM * kBlockK : kTileM * kBlockK;
   static constexpr int kStageBytes = kWBytes + kTokBytes;
   static constexpr int kStages = kMode == kGemm1 ? 6 : 11;
-  // TMEM groups in the 256 allocated columns: GEMM1 groups hold the X1 and X2
-  // chains (2 x 16 columns), GEMM2 groups 16 columns.
+  // One TMEM group per K block, 2 x 16 columns: the X1 and X2 chains in GEMM1,
+  // the two 64-deep halves in GEMM2; 16 groups in the 512 allocated columns.
   static constexpr int kBufCols = 2 * kSmallN;
   static constexpr int kBufs = kSmallTmemCols / kBufCols;
+  static_assert(kBufs <= kSmallBufsMax, "TMEM groups exceed the barrier slots");
 };
 
 template <int kMode>
