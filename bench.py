@@ -64,6 +64,13 @@ def parse():
     return ap.parse_args()
 
 
+# DRAM bytes (read + write) of one GEMM1 launch from the committed full ncu
+# capture of the same-density 32-local-expert case; weights dominate, so a
+# launch over more experts moves that many times more.
+GEMM1_E32_DRAM_BYTES = (969.4 + 20.6) * 1e6
+GEMM1_E32_ACTIVE = 32
+
+
 def load_peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
@@ -327,7 +334,12 @@ def run_ours(a):
         "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
         "frac": round(g1_flops / (g1_ms * 1e-3) / 1e12 / fp8_peak, 3),
         "peak_kind": "measured on this GPU: cuBLAS FP8 e4m3 8192^3 (torch._scaled_mm)",
-        "traffic": None,
+        "traffic": round(GEMM1_E32_DRAM_BYTES * active / GEMM1_E32_ACTIVE),
+        "traffic_unit": "bytes per launch",
+        "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one GEMM1 launch "
+                           f"on the 32-local-expert case (same rows per expert), scaled by active "
+                           f"experts {active}/{GEMM1_E32_ACTIVE} "
+                           f"(profiles/moe_gemm_kernel_dsv3_e32_t8192_full.md)"),
         "hbm_view": {"achieved_gbs": round(g1_bytes / (g1_ms * 1e-3) / 1e9, 1),
                      "peak_gbs": peaks["hbm_gbs"], "peak_kind": peak_kind,
                      "frac": round(g1_bytes / (g1_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)},
