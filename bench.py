@@ -12,20 +12,28 @@ definition's shapes and distributions (``moe_b200.workloads``); the weights
 
 A step is one full ``moe_fp8_forward``: routing, dispatch, GEMM1 + SwiGLU +
 requant, GEMM2 + weighted scatter-add, bf16 cast.  ``value`` is tokens/s with
-all inputs resident in HBM; ``e2e`` is the same metric through the public
-``run()`` with the step's activations copied from pinned host memory and the
-bf16 output read back every step.  Extra keys report decode latency (T=1..64),
-the reference's contest shape (32 of 256 experts) next to its published
-latencies, and per-kernel timings from CUDA events recorded by the library on
-the launching stream.
+all inputs resident in HBM (K plain forwards between two events); the per-stage
+times come from K more forwards with events recorded by the library between
+its kernels.  ``e2e`` is the same metric through the public ``run()`` with
+every step's activations copied from pinned host memory and its bf16 output
+copied back, the copies on their own streams so that they overlap the
+neighbouring steps' compute (double-buffered, as a serving loop would).
+
+Extra keys: the other prefill sizes of config 2 (T=1024/4096/16384), config 3
+(Zipf-skewed routing, T=8192) with its realised expert histogram, config 4 on
+one GPU (4096 bf16 tokens quantised on the GPU, uniform routing), decode
+latency (config 1, T=1..64), the reference's contest shape (32 of 256 experts)
+next to its published latencies and to FlashInfer's
+``trtllm_fp8_block_scale_moe`` timed as a black box on the same GPU and inputs.
 
 ``--impl reference`` times the CPU restatement of the reference algorithm
 (``oracle/``) on the host cores, on a bounded sample of the same workload.
 
-Under ``torchrun`` (N>1) every rank runs the expert-parallel layer: 256
-experts sharded contiguously, T tokens per rank, NCCL all-to-all dispatch and
-combine (``moe_b200.ep``); value = all ranks' tokens / max over ranks of the
-step time.
+Under ``torchrun`` (N>1) every rank runs the expert-parallel layer (config 4:
+256 experts sharded contiguously, 4096 bf16 tokens per rank, uniform routing)
+with dispatch and combine by the library's NVLink kernels; value = all ranks'
+tokens / max over ranks of the step time.  Before timing, a sample of every
+rank's output rows is checked against the single-GPU layer (``parity``).
 """
 from __future__ import annotations
 
@@ -45,6 +53,9 @@ NOMINAL_FP8_TFLOPS = 4500.0
 # Published latencies of the reference at the contest shape (32 local experts),
 # writeup.pdf p3 Table 1, ms.
 REF_PUBLISHED_MS = {1: 0.636, 7: 0.668, 80: 0.968, 901: 1.046, 11984: 2.579, 14107: 3.440}
+# The FlashInfer baseline of the writeup's speed-up column, derived from the
+# same table (reference ms x its published speed-up over FlashInfer).
+FLASHINFER_IMPLIED_MS = {1: 0.064, 7: 0.094, 80: 0.271, 901: 0.701, 11984: 4.977, 14107: 6.364}
 
 
 def parse():
@@ -56,17 +67,21 @@ def parse():
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default 8192 at N=1, 4096 per GPU under EP)")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip decode / contest / e2e / cpu-baseline extras")
-    ap.add_argument("--cpu-sample-tokens", type=int, default=16)
+                    help="skip the extra configurations, e2e and the cpu baseline")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=4)
     ap.add_argument("--e-local", type=int, default=256,
                     help="local experts (0..e_local-1 of 256); < 256 gives the small "
                          "same-density case used for ncu captures")
+    ap.add_argument("--zipf", type=float, default=None,
+                    help="headline run with Zipf(s)-skewed routing (config 3) instead")
+    ap.add_argument("--flashinfer-contest", action="store_true", help=argparse.SUPPRESS)
     return ap.parse_args()
 
 
-# DRAM bytes (read + write) of one GEMM1 launch from the committed full ncu
-# capture of the same-density 32-local-expert case; weights dominate, so a
-# launch over more experts moves that many times more.
+# DRAM bytes (read + write) of one GEMM1 launch, ncu dram__bytes_read.sum +
+# dram__bytes_write.sum, measured on the same-density 32-local-expert case
+# (T=8192 tokens routed over 256 experts, experts 0-31 local); weights
+# dominate, so a launch over more experts moves that many times more.
 GEMM1_E32_DRAM_BYTES = (969.4 + 20.6) * 1e6
 GEMM1_E32_ACTIVE = 32
 
@@ -171,14 +186,30 @@ def algorithmic_bytes(shape, counts_active, t):
             t * (h + 4 * (h // 128) + 4 * shape.e_global + 2 * h))
 
 
+WEIGHT_KEYS = ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")
+
+
+def layer_inputs(weights, shape, seed, zipf=None, zero_bias=False):
+    """Token-side inputs for ``shape`` (seeded) combined with shared weights; the
+    weights' first ``shape.e_local`` experts are the local ones."""
+    from moe_b200 import workloads
+    inp = workloads.make_inputs(shape, seed=seed, device="cuda", zipf=zipf, weights=False)
+    for k in WEIGHT_KEYS:
+        inp[k] = weights[k][:shape.e_local]
+    if zero_bias:
+        inp["routing_bias"] = inp["routing_bias"].zero_()
+    return inp
+
+
 class Runner:
     """Holds inputs, workspace and events for repeated forwards of one shape."""
 
-    def __init__(self, torch, shape, seed=0, zipf=None):
-        from moe_b200 import api, workloads, _lib
+    def __init__(self, torch, shape, inp):
+        from moe_b200 import api, _lib
         self.torch, self.api, self._lib, self.shape = torch, api, _lib, shape
-        self.inp = workloads.make_inputs(shape, seed=seed, device="cuda", zipf=zipf)
+        self.inp = inp
         self.out = torch.empty(shape.t, shape.hidden, dtype=torch.bfloat16, device="cuda")
+        from moe_b200 import workloads
         self.args, self.keep, _ = api.build_args(*workloads.run_args(self.inp), self.out,
                                                  shape.n_group, shape.topk_group, shape.top_k)
         lay = api.workspace_layout(self.args)
@@ -187,7 +218,6 @@ class Runner:
         self.args.workspace_bytes = lay.total_bytes
         self.lib = _lib.load()
         self.stream = torch.cuda.current_stream()
-        self.events = []
 
     def forward(self, events=None):
         import ctypes
@@ -213,45 +243,64 @@ class Runner:
         torch.cuda.synchronize()
         return evs
 
+    def views(self):
+        return self.api.workspace_views(self.args, self.ws)
+
     def active_experts(self):
-        return int((self.api.workspace_views(self.args, self.ws)["counts"] > 0).sum().item())
+        return int((self.views()["counts"] > 0).sum().item())
+
+    def assignments(self):
+        return int(self.views()["counts"].sum().item())
 
 
-def time_steps(torch, runner, steps, warmup, profile=True, flush=None):
+STAGES = ["route", "permute", "gemm1", "gemm2", "finalize"]
+
+
+def time_plain(torch, runner, steps, warmup):
+    """ms per forward over ``steps`` back-to-back forwards (no per-stage events)."""
     for _ in range(warmup):
         runner.forward()
     torch.cuda.synchronize()
-    evs = runner.make_events(steps) if profile else None
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    per_step = []
-    if flush is None:
-        start.record()
-        for i in range(steps):
-            runner.forward(evs[i] if profile else None)
-        end.record()
-        torch.cuda.synchronize()
-        total = start.elapsed_time(end)
-    else:
-        total = 0.0
-        for i in range(steps):
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        runner.forward()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def time_stages(torch, runner, steps, flush=None):
+    """Mean per-stage ms from the library's stage events (one event row per step)."""
+    evs = runner.make_events(steps)
+    for i in range(steps):
+        if flush is not None:
             flush()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            runner.forward(evs[i] if profile else None)
-            e.record()
-            e.synchronize()
-            per_step.append(s.elapsed_time(e))
-            total += per_step[-1]
-    stages = None
-    if profile:
-        names = ["route", "permute", "gemm1", "gemm2", "finalize"]
-        stages = {n: statistics.mean(row[j].elapsed_time(row[j + 1]) for row in evs)
-                  for j, n in enumerate(names)}
-    return total / steps, stages, per_step
+        runner.forward(evs[i])
+    torch.cuda.synchronize()
+    return {n: statistics.mean(row[j].elapsed_time(row[j + 1]) for row in evs)
+            for j, n in enumerate(STAGES)}
+
+
+def prefill_point(torch, runner, steps, warmup, fp8_peak):
+    from moe_b200 import workloads
+    ms = time_plain(torch, runner, steps, warmup)
+    st = time_stages(torch, runner, max(3, steps // 2))
+    n_assign = runner.assignments()
+    flops = n_assign * workloads.flops_per_assignment(runner.shape)
+    tf = flops / (ms * 1e-3) / 1e12
+    g1 = n_assign * 4 * runner.shape.hidden * runner.shape.inter / (st["gemm1"] * 1e-3) / 1e12
+    g2 = n_assign * 2 * runner.shape.hidden * runner.shape.inter / (st["gemm2"] * 1e-3) / 1e12
+    return {"ms": round(ms, 4), "tokens_per_s": round(runner.shape.t / (ms * 1e-3), 1),
+            "tflops": round(tf, 1), "fp8_frac_measured": round(tf / fp8_peak, 3),
+            "fp8_frac_nominal": round(tf / NOMINAL_FP8_TFLOPS, 3),
+            "gemm1_tflops": round(g1, 1), "gemm2_tflops": round(g2, 1),
+            "stage_ms": {k: round(v, 4) for k, v in st.items()},
+            "active_experts": runner.active_experts()}
 
 
 # ----------------------------------------------------------------------------
-# arms
+# CPU baseline (the oracle port)
 # ----------------------------------------------------------------------------
 
 def cpu_baseline(shape, inp_gpu, sample_tokens, torch):
@@ -291,37 +340,44 @@ def cpu_baseline(shape, inp_gpu, sample_tokens, torch):
     return t / dt, dt, t, threads
 
 
+# ----------------------------------------------------------------------------
+# our arm, one GPU
+# ----------------------------------------------------------------------------
+
 def run_ours(a):
     import torch
     from moe_b200 import workloads
-    rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1:
         return run_ep(a)
     torch.cuda.set_device(0)
     peaks, peak_kind = load_peaks()
     t = a.tokens or 8192
+    full = workloads.dsv3_shape(t)
+    weights = workloads.make_inputs(full, seed=0, device="cuda")   # tokens of seed 0 + all weights
     shape = workloads.dsv3_shape(t, e_local=a.e_local)
-    runner = Runner(torch, shape, seed=0)
+    if a.zipf is None:
+        inp = {k: (v[:shape.e_local] if k in WEIGHT_KEYS else v) for k, v in weights.items()}
+    else:
+        inp = layer_inputs(weights, shape, seed=0, zipf=a.zipf)
+    runner = Runner(torch, shape, inp)
     clocks = ClockSampler(torch.cuda.current_device())
-    # timed region: K forwards with per-stage events
+    # timed region: K plain forwards
     for _ in range(a.warmup):
         runner.forward()
     torch.cuda.synchronize()
-    evs = runner.make_events(a.steps)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with clocks:
         start.record()
-        for i in range(a.steps):
-            runner.forward(evs[i])
+        for _ in range(a.steps):
+            runner.forward()
         end.record()
         torch.cuda.synchronize()
     ms = start.elapsed_time(end) / a.steps
-    names = ["route", "permute", "gemm1", "gemm2", "finalize"]
-    stages = {n: statistics.mean(row[j].elapsed_time(row[j + 1]) for row in evs)
-              for j, n in enumerate(names)}
+    # per-kernel times: K more forwards with the library's stage events
+    stages = time_stages(torch, runner, a.steps)
     active = runner.active_experts()
-    n_assign = int(runner.api.workspace_views(runner.args, runner.ws)["counts"].sum().item())
+    n_assign = runner.assignments()
     flops = n_assign * workloads.flops_per_assignment(shape)
     value = t / (ms * 1e-3)
     fp8_peak = fp8_cublas_peak_tflops(torch)
@@ -337,20 +393,21 @@ def run_ours(a):
         "traffic": round(GEMM1_E32_DRAM_BYTES * active / GEMM1_E32_ACTIVE),
         "traffic_unit": "bytes per launch",
         "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one GEMM1 launch "
-                           f"on the 32-local-expert case (same rows per expert), scaled by active "
-                           f"experts {active}/{GEMM1_E32_ACTIVE} "
-                           f"(profiles/moe_gemm_kernel_dsv3_e32_t8192_full.md)"),
+                           f"on the same-density 32-local-expert case (T=8192, experts 0-31 "
+                           f"local), scaled by active experts {active}/{GEMM1_E32_ACTIVE}"),
         "hbm_view": {"achieved_gbs": round(g1_bytes / (g1_ms * 1e-3) / 1e9, 1),
                      "peak_gbs": peaks["hbm_gbs"], "peak_kind": peak_kind,
                      "frac": round(g1_bytes / (g1_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)},
     }
+    cfg_name = "config 3, Zipf routing" if a.zipf is not None else \
+        ("config 2" if shape.e_local == 256 else "same-density subset")
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": 1,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp8-e4m3 x e4m3 -> fp32 (bf16 out)", "data": "synthetic (seeded, random-init weights)",
         "config": {"workload": f"DeepSeek-V3 MoE layer, T={t}, {shape.e_local} of 256 experts "
-                               f"on 1 GPU" + (" (config 2)" if shape.e_local == 256 else ""),
+                               f"on 1 GPU ({cfg_name})",
                    "model": "DeepSeek-V3 MoE layer", "global_batch": t, "seq_len": 1,
                    "hidden": shape.hidden, "intermediate": shape.inter, "experts": shape.e_local,
                    "top_k": 8, "parallelism": "single GPU",
@@ -370,12 +427,14 @@ def run_ours(a):
                               "basis": "max(FLOPs / measured FP8 cuBLAS, bytes / measured HBM)"}
     if not a.no_extras:
         line["e2e"] = e2e_run(torch, runner, a)
-        inp_gpu = runner.inp
         del runner
         torch.cuda.empty_cache()
-        line["decode"] = decode_sweep(torch, peaks)
-        line["contest_shape"] = contest_sweep(torch)
-        tps, dt, ns, threads = cpu_baseline(shape, inp_gpu, a.cpu_sample_tokens, torch)
+        line["prefill_sweep"] = prefill_sweep(torch, weights, fp8_peak, a)
+        line["zipf_t8192"] = zipf_run(torch, weights, fp8_peak, a)
+        line["ep_config_n1"] = ep_config_n1(torch, weights, a)
+        line["decode"] = decode_sweep(torch, weights, peaks)
+        line["contest_shape"] = contest_sweep(torch, weights)
+        tps, dt, ns, threads = cpu_baseline(full, weights, a.cpu_sample_tokens, torch)
         line["cpu_baseline"] = {"value": round(tps, 3), "unit": "tokens/s", "cores": threads,
                                 "kind": "port",
                                 "sample": f"first {ns} tokens of the T={t} batch through the numpy "
@@ -384,41 +443,141 @@ def run_ours(a):
 
 
 def e2e_run(torch, runner, a):
-    """Same metric through run(): activations from pinned host memory every step,
-    bf16 output read back to pinned host memory every step."""
-    from moe_b200 import run, workloads
+    """Same metric through run(): every step copies its activations from pinned
+    host memory and its bf16 output back to pinned host memory.  The copies run
+    on two copy streams with device buffers double-buffered by step parity, so
+    step i+1's inputs arrive and step i-1's output leaves while step i computes.
+    Timed from an event before the first input copy to an event after the last
+    output copy."""
+    from moe_b200 import run
     shape, inp = runner.shape, runner.inp
-    host = {k: inp[k].cpu().pin_memory() for k in
-            ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")}
-    out_host = torch.empty(shape.t, shape.hidden, dtype=torch.bfloat16).pin_memory()
-    args = workloads.run_args(inp)
-    args[0], args[1], args[2], args[3] = (host["routing_logits"], host["routing_bias"],
-                                          host["hidden_states"], host["hidden_states_scale"])
+    keys = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+    host = {k: inp[k].cpu().pin_memory() for k in keys}
+    out_host = [torch.empty(shape.t, shape.hidden, dtype=torch.bfloat16).pin_memory()
+                for _ in range(2)]
+    dev_in = [{k: torch.empty_like(inp[k]) for k in keys} for _ in range(2)]
+    dev_out = [torch.empty(shape.t, shape.hidden, dtype=torch.bfloat16, device="cuda")
+               for _ in range(2)]
+    weights = [inp[k] for k in WEIGHT_KEYS]
     kw = dict(n_group=shape.n_group, topk_group=shape.topk_group, top_k=shape.top_k)
-    for _ in range(max(3, a.warmup)):
-        run(*args, out_host, **kw)
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = lambda: torch.cuda.Event(enable_timing=False)   # noqa: E731
+    ready, done, freed = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    for e in freed + done:
+        e.record(comp)
+
+    def copy_in(b):
+        with torch.cuda.stream(h2d):
+            h2d.wait_event(done[b])             # the forward that read buffer b is over
+            for k in keys:
+                dev_in[b][k].copy_(host[k], non_blocking=True)
+            ready[b].record(h2d)
+
+    def steps_loop(n, t0=None):
+        if t0 is not None:
+            t0.record(h2d)
+        copy_in(0)
+        for i in range(n):
+            b = i & 1
+            if i + 1 < n:
+                copy_in(b ^ 1)
+            comp.wait_event(ready[b])
+            comp.wait_event(freed[b])           # buffer b's previous output has left
+            args = [dev_in[b][k] for k in keys] + weights + \
+                [inp["local_expert_offset"], inp["routed_scaling_factor"]]
+            run(*args, dev_out[b], **kw)
+            done[b].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done[b])
+                out_host[b].copy_(dev_out[b], non_blocking=True)
+                freed[b].record(d2h)
+
+    steps_loop(max(3, a.warmup))
     torch.cuda.synchronize()
     steps = max(5, a.steps // 2)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(steps):
-        run(*args, out_host, **kw)
-    t1.record()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps_loop(steps, t0)
+    t1.record(d2h)
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / steps
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    h2d_bytes = sum(v.numel() * v.element_size() for v in host.values())
     return {"value": round(shape.t / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4),
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": shape.t * shape.hidden * 2,
-            "path": "moe_b200.run() with pinned host activations and host output"}
+            "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": shape.t * shape.hidden * 2,
+            "path": "moe_b200.run() on device buffers filled from pinned host memory each step; "
+                    "copies on two copy streams, double-buffered, overlapping compute"}
 
 
-def decode_sweep(torch, peaks):
-    """Decode latency (T=1..64, all 256 experts), L2 flushed before every step:
-    p50 of the eager forward (three kernels at T <= 2, four up to T=16, two
-    memsets and five kernels above; no per-stage events), p50 of the
-    same forward replayed as one CUDA graph (``moe_b200.LayerGraph``), and a
-    per-stage breakdown from a separate run with stage events."""
+def prefill_sweep(torch, weights, fp8_peak, a):
+    """Config 2 at the other token counts (all 256 experts, uniform routing)."""
+    from moe_b200 import workloads
+    res = {}
+    for t in (1024, 4096, 16384):
+        shape = workloads.dsv3_shape(t)
+        r = Runner(torch, shape, layer_inputs(weights, shape, seed=30 + t))
+        res[str(t)] = prefill_point(torch, r, 10, 3, fp8_peak)
+        del r
+        torch.cuda.empty_cache()
+    return res
+
+
+def zipf_run(torch, weights, fp8_peak, a, s=1.2):
+    """Config 3: T=8192 with expert popularity ~ Zipf(1.2) over a random
+    permutation of the experts (realised through the router bias)."""
+    from moe_b200 import workloads
+    shape = workloads.dsv3_shape(8192)
+    r = Runner(torch, shape, layer_inputs(weights, shape, seed=3, zipf=s))
+    res = prefill_point(torch, r, 10, 3, fp8_peak)
+    counts = r.views()["counts"].float()
+    res["zipf_s"] = s
+    res["histogram"] = {"max_over_mean": round(float(counts.max() / counts.mean()), 2),
+                        "zero_experts": int((counts == 0).sum().item()),
+                        "max_rows": int(counts.max().item()),
+                        "mean_rows": round(float(counts.mean()), 1)}
+    del r
+    torch.cuda.empty_cache()
+    return res
+
+
+def ep_config_n1(torch, weights, a):
+    """Config 4 on one GPU: 4096 bf16 tokens quantised 1x128 on the GPU every
+    step, then the layer with all 256 experts, uniform routing (zero bias) --
+    the per-GPU work of the expert-parallel runs, for v_N / (N * this)."""
+    from moe_b200 import quantize_1x128, workloads
+    t = 4096
+    shape = workloads.dsv3_shape(t)
+    inp = layer_inputs(weights, shape, seed=1000, zero_bias=True)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2000)
+    x = torch.randn(t, shape.hidden, generator=g, device="cuda").to(torch.bfloat16)
+    r = Runner(torch, shape, inp)
+    q, sc = inp["hidden_states"], inp["hidden_states_scale"]
+
+    def step():
+        quantize_1x128(x, q, sc)
+        r.forward()
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(a.steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / a.steps
+    res = {"tokens_per_s": round(t / (ms * 1e-3), 1), "ms": round(ms, 4), "tokens": t,
+           "routing": "uniform (zero bias)", "active_experts": r.active_experts()}
+    del r
+    torch.cuda.empty_cache()
+    return res
+
+
+def decode_sweep(torch, weights, peaks):
+    """Decode latency (config 1, T=1..64, all 256 experts), L2 flushed before
+    every step: p50 of the eager forward, p50 of the same forward replayed as
+    one CUDA graph (``moe_b200.LayerGraph``), and a per-stage breakdown from a
+    separate run with stage events."""
     from moe_b200 import workloads, LayerGraph
     res = {}
     flush_buf = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
@@ -441,8 +600,9 @@ def decode_sweep(torch, peaks):
         return statistics.median(per)
     for t in (1, 8, 32, 64):
         shape = workloads.dsv3_shape(t)
-        r = Runner(torch, shape, seed=1)
-        _, stages, _ = time_steps(torch, r, 10, 3, profile=True, flush=flush)
+        r = Runner(torch, shape, layer_inputs(weights, shape, seed=1))
+        r.forward()
+        stages = time_stages(torch, r, 10, flush=flush)
         eager = p50_of(lambda: r.forward())
         out_g = torch.empty_like(r.out)
         graph = LayerGraph(*workloads.run_args(r.inp), out_g)
@@ -461,26 +621,157 @@ def decode_sweep(torch, peaks):
     return res
 
 
-def contest_sweep(torch):
-    """The reference's published shape: 32 local experts of 256."""
+def flashinfer_forward(inp, shape):
+    """FlashInfer's trtllm_fp8_block_scale_moe (closed kernels, run as a black
+    box) on the reference's inputs: DeepSeek-V3 routing, DeepSeekFp8 block
+    scales, K-major weights."""
+    from flashinfer.fused_moe import trtllm_fp8_block_scale_moe
+    return trtllm_fp8_block_scale_moe(
+        inp["routing_logits"], inp["routing_bias"], inp["hidden_states"],
+        inp["hidden_states_scale"], inp["gemm1_weights"], inp["gemm1_weights_scale"],
+        inp["gemm2_weights"], inp["gemm2_weights_scale"], shape.e_global, shape.top_k,
+        shape.n_group, shape.topk_group, shape.inter, shape.local_expert_offset, shape.e_local,
+        shape.routed_scaling_factor, routing_method_type=2)
+
+
+CONTEST_TOKENS = (1, 7, 80, 901, 11984, 14107)
+
+
+def contest_inputs(torch, n, weights):
     from moe_b200 import workloads
+    shape = workloads.dsv3_shape(n, e_local=32, local_expert_offset=0)
+    return shape, layer_inputs(weights, shape, seed=2)
+
+
+def contest_weights():
+    """The first 32 experts of the N=1 run's layer (the same generator draws)."""
+    from moe_b200 import workloads
+    return workloads.make_inputs(workloads.dsv3_shape(8192, e_local=32), seed=0, device="cuda")
+
+
+def run_flashinfer_contest():
+    """Child process of the contest sweep: FlashInfer's kernel on the contest
+    inputs, timed like ours, plus the cosine of its output against ours.
+    Prints one JSON dict {n: {...}}; an exception is reported as a string."""
+    import torch
+    torch.cuda.set_device(0)
+    weights = contest_weights()
     res = {}
-    for n in (1, 7, 80, 901, 11984, 14107):
-        shape = workloads.dsv3_shape(n, e_local=32, local_expert_offset=0)
-        r = Runner(torch, shape, seed=2)
-        ms, _, _ = time_steps(torch, r, 20, 5, profile=False)
+    for n in CONTEST_TOKENS:
+        shape, inp = contest_inputs(torch, n, weights)
+        try:
+            fo = flashinfer_forward(inp, shape)
+            for _ in range(5):
+                flashinfer_forward(inp, shape)
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(20):
+                flashinfer_forward(inp, shape)
+            e.record()
+            torch.cuda.synchronize()
+            fms = s.elapsed_time(e) / 20
+            r = Runner(torch, shape, inp)
+            r.forward()
+            torch.cuda.synchronize()
+            a_, b_ = r.out.float().flatten(), fo.float().flatten()
+            cos = float(torch.dot(a_, b_) / (a_.norm() * b_.norm() + 1e-30))
+            res[str(n)] = {"ms": round(fms, 4), "cos_vs_ours": round(cos, 6)}
+            del r
+        except Exception as exc:  # noqa: BLE001 - reported to the parent
+            res[str(n)] = f"{type(exc).__name__}: {str(exc)[:300]}"
+            break
+    print("FLASHINFER_JSON " + json.dumps(res))
+
+
+def flashinfer_contest_child():
+    import subprocess
+    try:
+        p = subprocess.run([sys.executable, os.path.abspath(__file__), "--flashinfer-contest"],
+                           capture_output=True, text=True, timeout=600)
+    except subprocess.TimeoutExpired:
+        return None, "timed out after 600 s"
+    for line in p.stdout.splitlines():
+        if line.startswith("FLASHINFER_JSON "):
+            return json.loads(line[len("FLASHINFER_JSON "):]), None
+    tail = (p.stderr or p.stdout or "").strip().splitlines()[-1:] or ["no output"]
+    return None, f"exit {p.returncode}: {tail[0][:300]}"
+
+
+def contest_sweep(torch, weights):
+    """The reference's published shape (32 local experts of 256): our layer,
+    the reference's published latency, and FlashInfer's kernel timed on the same
+    GPU and inputs in a child process (black box; its output is compared with
+    ours there)."""
+    res = {}
+    for n in CONTEST_TOKENS:
+        shape, inp = contest_inputs(torch, n, weights)
+        r = Runner(torch, shape, inp)
+        ms = time_plain(torch, r, 20, 5)
         res[str(n)] = {"ms": round(ms, 4), "reference_published_ms": REF_PUBLISHED_MS[n],
-                       "speedup_vs_published": round(REF_PUBLISHED_MS[n] / ms, 2)}
+                       "speedup_vs_published": round(REF_PUBLISHED_MS[n] / ms, 2),
+                       "flashinfer_implied_published_ms": FLASHINFER_IMPLIED_MS[n]}
         del r
         torch.cuda.empty_cache()
+    fi, err = flashinfer_contest_child()
+    for n in CONTEST_TOKENS:
+        row = res[str(n)]
+        got = fi.get(str(n)) if fi else None
+        if isinstance(got, dict):
+            row["flashinfer_ms"] = got["ms"]
+            row["speedup_vs_flashinfer"] = round(got["ms"] / row["ms"], 2)
+            row["cos_vs_flashinfer"] = got["cos_vs_ours"]
+        else:
+            row["flashinfer"] = f"unavailable: {got or err}"
     return res
+
+
+# ----------------------------------------------------------------------------
+# expert parallel (N > 1)
+# ----------------------------------------------------------------------------
+
+def ep_parity(torch, dist, layer, inp, bias, x_bf16, wts, world, rank, lo, shape, sample=8):
+    """Each rank's EP output for its first ``sample`` tokens against the layer
+    computed shard by shard with ``run()`` (the reference's own API for an
+    expert shard: local_expert_offset + the rank's weight slice): every rank runs
+    its shard on all ranks' sample tokens, the fp32 partials are summed over the
+    ranks, and each rank compares its own rows.  Same tolerance as the tests."""
+    from moe_b200 import quantize_1x128, run
+    out = torch.empty(x_bf16.shape[0], shape.hidden, dtype=torch.bfloat16, device="cuda")
+    layer.forward_bf16(inp["routing_logits"], bias, x_bf16, *wts, shape.routed_scaling_factor,
+                       out)
+    q, s = quantize_1x128(x_bf16[:sample].contiguous())
+    lg = inp["routing_logits"][:sample].contiguous()
+    all_q = torch.empty(world * sample, shape.hidden, dtype=torch.uint8, device="cuda")
+    all_l = torch.empty(world * sample, shape.e_global, dtype=torch.float32, device="cuda")
+    all_s = torch.empty(world * sample, shape.hidden // 128, dtype=torch.float32, device="cuda")
+    dist.all_gather_into_tensor(all_q, q.view(torch.uint8))
+    dist.all_gather_into_tensor(all_l, lg)
+    dist.all_gather_into_tensor(all_s, s.t().contiguous())
+    part = torch.empty(world * sample, shape.hidden, dtype=torch.bfloat16, device="cuda")
+    run(all_l, bias, all_q.view(torch.float8_e4m3fn), all_s.t().contiguous(), *wts, lo,
+        shape.routed_scaling_factor, part)
+    ref = part.float()
+    dist.all_reduce(ref)
+    mine = ref[rank * sample:(rank + 1) * sample]
+    got = out[:sample].float()
+    err = (got - mine).abs().max()
+    tol_ok = bool(((got - mine).abs() <= 1e-2 + 2e-2 * mine.abs()).all().item())
+    cos = torch.dot(got.flatten(), mine.flatten()) / (got.norm() * mine.norm() + 1e-30)
+    stats = torch.tensor([err.item(), -cos.item(), 0.0 if tol_ok else 1.0], device="cuda")
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ok = stats[2].item() == 0.0 and -stats[1].item() >= 0.9999
+    return {"ok": ok, "max_abs_err": round(stats[0].item(), 5), "min_cos": round(-stats[1].item(), 7),
+            "sample_tokens_per_rank": sample,
+            "reference": "sum over ranks of run() on the rank's expert slice (fp32 sum of the "
+                         "bf16 shard outputs), same tolerance as the tests"}
 
 
 def run_ep(a):
     """Expert-parallel layer over all ranks (config 4): 256 experts sharded
-    contiguously, ``a.tokens`` (default 4096) tokens per rank, NCCL all-to-all
-    dispatch and combine.  value = all ranks' tokens / max over ranks of the
-    device-timed step."""
+    contiguously, ``a.tokens`` (default 4096) bf16 tokens per rank quantised on
+    the GPU every step, uniform routing (zero router bias).  value = all ranks'
+    tokens / max over ranks of the device-timed step."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -496,10 +787,10 @@ def run_ep(a):
     shape = workloads.dsv3_shape(t, e_local=per, local_expert_offset=lo)
     inp = workloads.make_inputs(shape, seed=1000 + rank, device="cuda")
     shared = workloads.make_inputs(workloads.dsv3_shape(1), seed=7, device="cuda", weights=False)
-    inp["routing_bias"] = shared["routing_bias"]          # one bias for the whole layer
+    uniform_bias = torch.zeros_like(shared["routing_bias"])   # config 4: uniform routing
+    skewed_bias = shared["routing_bias"]                      # N(0, 0.1), shared by the ranks
     out = torch.empty(t, shape.hidden, dtype=torch.bfloat16, device="cuda")
-    wts = [inp[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights",
-                            "gemm2_weights_scale")]
+    wts = [inp[k] for k in WEIGHT_KEYS]
 
     # Config 4 starts from bf16 N(0,1) activations: every step quantises them to
     # e4m3 1x128 on the GPU before the FP8 dispatch.
@@ -510,52 +801,47 @@ def run_ep(a):
     # Dispatch and combine are the library's own NVLink kernels (moe_b200.ep.FusedEP);
     # NCCL only all-gathers row counts and orders the phases.
     layer = ep.FusedEP(t, shape.hidden, shape.inter, 256)
+    parity = ep_parity(torch, dist, layer, inp, uniform_bias, x_bf16, wts, world, rank, lo, shape)
 
     stage_names = ["send_plan", "count_allgather", "dispatch", "barrier1", "experts_combine",
                    "barrier2", "finalize"]
 
-    def step(logits, x, o, tim=None):
+    def step(bias, logits, x, o, tim=None):
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(8)] if tim is not None else None
-        layer.forward_bf16(logits, inp["routing_bias"], x, *wts, shape.routed_scaling_factor, o,
-                           events=evs)
+        layer.forward_bf16(logits, bias, x, *wts, shape.routed_scaling_factor, o, events=evs)
         if tim is not None:
-            tim["send_cnt"] = layer.send_cnt
             tim.setdefault("events", []).append(evs)
 
-    dev_in = (inp["routing_logits"], x_bf16)
-    for _ in range(a.warmup):
-        step(*dev_in, out)
-    torch.cuda.synchronize()
-    dist.barrier()
-    clocks = ClockSampler(local)
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    tim = {}
-    with clocks:
-        s.record()
-        for _ in range(a.steps):
-            step(*dev_in, out, tim)
-        e.record()
+    def timed(bias, steps, warmup, tim=None, clocks=None):
+        for _ in range(warmup):
+            step(bias, inp["routing_logits"], x_bf16, out)
         torch.cuda.synchronize()
-    ms = torch.tensor([s.elapsed_time(e) / a.steps], device="cuda")
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    # e2e: activations from pinned host memory and the output back to it, every step
-    host = [x.cpu().pin_memory() for x in dev_in]
-    out_host = torch.empty(t, shape.hidden, dtype=torch.bfloat16).pin_memory()
-    dist.barrier()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    steps2 = max(3, a.steps // 2)
-    s2.record()
-    for _ in range(steps2):
-        d = [x.to("cuda", non_blocking=True) for x in host]
-        step(*d, out)
-        out_host.copy_(out, non_blocking=True)
-    e2.record()
-    torch.cuda.synchronize()
-    ms2 = torch.tensor([s2.elapsed_time(e2) / steps2], device="cuda")
-    dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        import contextlib
+        with (clocks or contextlib.nullcontext()):
+            s.record()
+            for _ in range(steps):
+                step(bias, inp["routing_logits"], x_bf16, out, tim)
+            e.record()
+            torch.cuda.synchronize()
+        ms = torch.tensor([s.elapsed_time(e) / steps], device="cuda")
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    clocks = ClockSampler(local)
+    ms_v = timed(uniform_bias, a.steps, a.warmup, clocks=clocks)
+    rows_recv = layer.cnt_all.view(world, world).sum(0).tolist()
+    tim = {}
+    timed(uniform_bias, max(3, a.steps // 2), 1, tim=tim)
+    stage_ms = {n: round(statistics.mean(ev[j].elapsed_time(ev[j + 1]) for ev in tim["events"]), 4)
+                for j, n in enumerate(stage_names)}
+    rows_sent = int(layer.send_cnt.sum().item())
+    ms_skew = timed(skewed_bias, max(3, a.steps // 2), 2)
+    rows_recv_skew = layer.cnt_all.view(world, world).sum(0).tolist()
+    ms2 = ep_e2e(torch, dist, layer, inp, uniform_bias, x_bf16, wts, shape, t, a)
     dist.barrier()
     if rank == 0:
-        ms_v, ms2_v = float(ms.item()), float(ms2.item())
         line = {
             "metric": METRIC, "value": round(world * t / (ms_v * 1e-3), 1), "unit": "tokens/s",
             "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_v, 4),
@@ -564,31 +850,95 @@ def run_ep(a):
             "data": "synthetic (seeded, random-init weights)",
             "config": {"workload": f"DeepSeek-V3 MoE layer, expert parallel over {world} GPUs, "
                                    f"{t} tokens per GPU of bf16 activations quantised 1x128 "
-                                   f"on the GPU each step (config 4)",
+                                   f"on the GPU each step, uniform routing (config 4)",
                        "model": "DeepSeek-V3 MoE layer", "global_batch": world * t, "seq_len": 1,
                        "experts_per_gpu": per,
                        "parallelism": f"ep{world} (dispatch and combine by NVLink peer stores "
                                       f"from the library's kernels; NCCL for counts and barriers)",
                        "l2": "weights > L2 (no flush needed)"},
-            "rows_sent_rank0": int(tim["send_cnt"].sum().item()) if "send_cnt" in tim else None,
+            "parity": parity,
+            "rows_sent_rank0": rows_sent,
             # rows each rank receives (sum over sources of cnt_all[source][rank]): the
             # slowest rank sets the step time
-            "rows_received_per_rank": layer.cnt_all.view(world, world).sum(0).tolist(),
-            "stage_ms_rank0": {n: round(statistics.mean(ev[j].elapsed_time(ev[j + 1])
-                                                        for ev in tim["events"]), 4)
-                               for j, n in enumerate(stage_names)} if tim.get("events") else None,
+            "rows_received_per_rank": rows_recv,
+            "stage_ms_rank0": stage_ms,
+            "ep_skewed": {"value": round(world * t / (ms_skew * 1e-3), 1),
+                          "ms_per_step": round(ms_skew, 4),
+                          "routing": "router bias N(0, 0.1) shared by all ranks",
+                          "rows_received_per_rank": rows_recv_skew},
             "clocks": clocks.summary(),
-            "e2e": {"value": round(world * t / (ms2_v * 1e-3), 1), "unit": "tokens/s",
-                    "ms_per_step": round(ms2_v, 4),
-                    "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in host),
+            "e2e": {"value": round(world * t / (ms2 * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(ms2, 4),
+                    "h2d_bytes_per_step": t * (shape.hidden * 2 + shape.e_global * 4),
                     "d2h_bytes_per_step": t * shape.hidden * 2,
-                    "path": "moe_b200.ep.FusedEP.forward_bf16 with pinned host activations and output"},
+                    "path": "moe_b200.ep.FusedEP.forward_bf16 on device buffers filled from pinned "
+                            "host memory each step; copies on two copy streams, double-buffered"},
             "gpu_launches": 11 * a.steps,
         }
         print(json.dumps(line))
     layer.close()
     dist.destroy_process_group()
 
+
+def ep_e2e(torch, dist, layer, inp, bias, x_bf16, wts, shape, t, a):
+    """EP step time with every step's activations (bf16) and logits copied from
+    pinned host memory and its output copied back, copies double-buffered on
+    their own streams; max over ranks."""
+    keys = ("routing_logits", "x")
+    host = {"routing_logits": inp["routing_logits"].cpu().pin_memory(),
+            "x": x_bf16.cpu().pin_memory()}
+    dev_in = [{k: torch.empty_like(host[k], device="cuda") for k in keys} for _ in range(2)]
+    dev_out = [torch.empty(t, shape.hidden, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    out_host = [torch.empty(t, shape.hidden, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ready = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    for e in done + freed:
+        e.record(comp)
+
+    def copy_in(b):
+        with torch.cuda.stream(h2d):
+            h2d.wait_event(done[b])
+            for k in keys:
+                dev_in[b][k].copy_(host[k], non_blocking=True)
+            ready[b].record(h2d)
+
+    def loop(n, t0=None):
+        if t0 is not None:
+            t0.record(h2d)
+        copy_in(0)
+        for i in range(n):
+            b = i & 1
+            if i + 1 < n:
+                copy_in(b ^ 1)
+            comp.wait_event(ready[b])
+            comp.wait_event(freed[b])
+            layer.forward_bf16(dev_in[b]["routing_logits"], bias, dev_in[b]["x"], *wts,
+                               shape.routed_scaling_factor, dev_out[b])
+            done[b].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done[b])
+                out_host[b].copy_(dev_out[b], non_blocking=True)
+                freed[b].record(d2h)
+
+    loop(2)
+    torch.cuda.synchronize()
+    dist.barrier()
+    steps = max(3, a.steps // 2)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    loop(steps, t0)
+    t1.record(d2h)
+    torch.cuda.synchronize()
+    ms = torch.tensor([t0.elapsed_time(t1) / steps], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return float(ms.item())
+
+
+# ----------------------------------------------------------------------------
+# reference arm
+# ----------------------------------------------------------------------------
 
 def run_reference(a):
     """CPU arm: the oracle restatement of the reference algorithm on host cores."""
@@ -598,7 +948,6 @@ def run_reference(a):
     import torch
     from moe_b200 import workloads
     t = a.tokens or 8192
-    shape = workloads.dsv3_shape(t)
     torch.set_num_threads(os.cpu_count() or 1)
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     sample = min(a.cpu_sample_tokens, t)
@@ -607,6 +956,7 @@ def run_reference(a):
     sshape = workloads.dsv3_shape(sample)
     inp = workloads.make_inputs(sshape, seed=0, device=dev)
     times = []
+    threads = os.cpu_count() or 1
     for i in range(a.warmup + a.steps):
         tps, dt, ns, threads = cpu_baseline(sshape, inp, sample, torch)
         if i >= a.warmup:
@@ -632,7 +982,9 @@ def run_reference(a):
 
 def main():
     a = parse()
-    if a.impl == "reference":
+    if a.flashinfer_contest:
+        run_flashinfer_contest()
+    elif a.impl == "reference":
         run_reference(a)
     else:
         run_ours(a)

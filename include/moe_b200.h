@@ -55,6 +55,20 @@ extern "C" {
 #define MOE_BIAS_BF16 1
 #define MOE_BIAS_F16 2
 
+/* MoeFwdArgs.flags */
+/* Fixed-order combine: GEMM2 stores every (token, expert) row's weighted fp32
+ * result and a gather adds a token's rows in routing-selection order, so the
+ * output is bit-identical from run to run.  The default adds rows with fp32
+ * atomics in whatever order they finish, as the reference does
+ * (kernel.py:246-250).  Costs one extra fp32 write and read per assignment row
+ * (rows_out in the workspace). */
+#define MOE_FLAG_DETERMINISTIC 0x1u
+/* Failure-detection tests only: the first MMA issuer of each GEMM1 CTA waits
+ * on a barrier that nothing completes, so its bounded wait runs out after
+ * wait_limit_ns; the layer then drains, records MOE_ERR_TIMEOUT (info = the
+ * wait site) and returns without faulting.  The output is not computed. */
+#define MOE_FLAG_TEST_STALL 0x100u
+
 typedef struct MoeFwdArgs {
   const float* routing_logits;
   const void* routing_bias;
@@ -78,6 +92,9 @@ typedef struct MoeFwdArgs {
   int32_t bias_dtype;          /* MOE_BIAS_* */
   void* workspace;             /* device scratch, 256-byte aligned */
   size_t workspace_bytes;
+  uint32_t flags;              /* MOE_FLAG_*; 0 = reference behaviour */
+  uint32_t reserved;           /* must be 0 */
+  uint64_t wait_limit_ns;      /* bound of every device-side wait; 0 = 2 s */
 } MoeFwdArgs;
 
 /* Offsets (bytes from the workspace base) of the per-stage buffers a forward
@@ -101,6 +118,8 @@ typedef struct MoeWorkspaceLayout {
   size_t inter;            /* [npad, I] e4m3     SwiGLU output, requantised */
   size_t inter_scale;      /* [I/64, npad] fp32  its per-64-column scales */
   size_t out_f32;          /* [T, H] fp32        scatter-add accumulator */
+  size_t assign_row;       /* [T, top_k] int32   permuted row of each assignment (-1: not local) */
+  size_t rows_out;         /* [npad, H] fp32     weighted GEMM2 rows (MOE_FLAG_DETERMINISTIC only) */
 } MoeWorkspaceLayout;
 
 /* Workspace bytes needed for the shape in `a` (pointers are not read).
@@ -153,9 +172,13 @@ int moe_fp8_device_error(const MoeFwdArgs* a, void* stream, int32_t* code, int32
  *
  * Scratch lives in a fixed device array inside the library (263,428 bytes) that
  * every GPU which loads the library keeps until the process exits.  Limits:
- * T <= 65536, E_global <= 256; larger sizes return MOE_ERR_TOO_LARGE.  The
- * first call on each device looks up that array's device address (with the
- * device current); make this first call before any stream capture.  All calls
+ * T <= 65536 (more tokens return MOE_ERR_TOO_LARGE); the router's shape rules
+ * (E_global <= 256 among them) are those of moe_fp8_forward and a violation
+ * returns MOE_ERR_SHAPE.  The first call on each device looks up that array's
+ * device address (with the device current) and keeps it for the life of the
+ * process; make this first call before any stream capture, and do not use the
+ * library across cudaDeviceReset (the kept address, like the kernels' shared
+ * memory settings, belongs to the context that reset destroys).  All calls
  * share the one array, so calls that overlap on the GPU (different streams,
  * or different host threads on the same device) race: order them on a
  * single stream. */

@@ -11,7 +11,12 @@
 namespace moe {
 namespace {
 
-constexpr int kLayoutSms = 148;   // token-per-block heuristic (B200 SM count)
+// The routing grid aims at this many blocks (8 warps each, a multiple of
+// 8 tokens per block): enough warps per SM to overlap the per-token shuffle
+// chains, few enough for the last block's scan over all block histograms, and
+// the bound the fixed scratch of moe_fp8_route_noalloc is sized for.
+constexpr int kRouteTargetBlocks = 256;
+constexpr int kLayoutSms = 148;   // B200 SM count: sizes the permute grid
 constexpr size_t kAlign = 1024;
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -40,13 +45,18 @@ int validate_shape(const MoeFwdArgs* a) {
   if (a->bias_dtype != MOE_BIAS_F32 && a->bias_dtype != MOE_BIAS_BF16 &&
       a->bias_dtype != MOE_BIAS_F16)
     return MOE_ERR_INVALID_ARG;
+  if ((a->flags & ~(MOE_FLAG_DETERMINISTIC | MOE_FLAG_TEST_STALL)) != 0 || a->reserved != 0)
+    return MOE_ERR_INVALID_ARG;
   return MOE_OK;
 }
+
+bool deterministic(const MoeFwdArgs* a) { return (a->flags & MOE_FLAG_DETERMINISTIC) != 0; }
 
 struct Layout {
   MoeWorkspaceLayout w;
   int tokens_per_block;
   int blocks;
+  int permute_split;   // permute blocks per routing block (grid.y)
 };
 
 // Decode-shaped batches (few rows per expert on average) take the
@@ -60,12 +70,19 @@ bool use_small_path(const MoeFwdArgs* a) {
 Layout make_layout(const MoeFwdArgs* a) {
   Layout L{};
   const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local, K = a->top_k;
-  int64_t tpw = (T + kLayoutSms * 8 - 1) / (kLayoutSms * 8);
+  int64_t tpw = (T + kRouteTargetBlocks * 8 - 1) / (kRouteTargetBlocks * 8);
   if (tpw < 1) tpw = 1;
   int64_t tpb = 8 * tpw;
   if (tpb > kMaxTokensPerBlock) tpb = kMaxTokensPerBlock;
   L.tokens_per_block = static_cast<int>(tpb);
   L.blocks = static_cast<int>((T + tpb - 1) / tpb);
+  // Permute blocks per routing block: about two blocks per SM in all, at
+  // least one assignment per warp.
+  int64_t split = (2 * kLayoutSms + L.blocks - 1) / (L.blocks > 0 ? L.blocks : 1);
+  const int64_t most = tpb * K / (kRouteThreads / 32);
+  if (split > most) split = most;
+  if (split < 1) split = 1;
+  L.permute_split = static_cast<int>(split);
   const int64_t nmax = T * (K < El ? K : El);
   const int64_t active = El < nmax ? El : nmax;
   int64_t tiles = (nmax + active * (kTileM - 1)) / kTileM;
@@ -94,6 +111,8 @@ Layout make_layout(const MoeFwdArgs* a) {
   w.inter = take(static_cast<size_t>(npad) * I);
   w.inter_scale = take(sizeof(float) * (I / kInterScaleBlock) * npad);
   w.out_f32 = take(sizeof(float) * T * H);
+  w.assign_row = take(sizeof(int) * T * K);
+  w.rows_out = take(deterministic(a) ? sizeof(float) * static_cast<size_t>(npad) * H : 0);
   w.total_bytes = off;
   return L;
 }
@@ -292,7 +311,11 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   pp.hs_scale = a->hidden_states_scale;
   pp.scale_ld = T;
   pp.T_dev = T_dev;
-  pp.zero_rows = T_dev ? out_f32 : nullptr;
+  const bool det = deterministic(a);
+  // the accumulator rows of the permute block's tokens (the deterministic
+  // combine stores rows instead of adding into the accumulator)
+  pp.zero_rows = det ? nullptr : out_f32;
+  pp.assign_row = ws_ptr<int>(a, w.assign_row);
   pp.row_token = ws_ptr<int>(a, w.row_token);
   pp.row_weight = ws_ptr<float>(a, w.row_weight);
   pp.a_perm = ws_ptr<uint8_t>(a, w.a_perm);
@@ -304,7 +327,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
     // its end.
     RouteParams rp = route_params(a, L, nullptr);
     rp.tokens_per_block = static_cast<int>(T);
-    const int64_t n4 = T * H / 4;
+    const int64_t n4 = det ? 0 : T * H / 4;
     int64_t zblocks = (n4 + 4 * kRouteThreads - 1) / (4 * kRouteThreads);
     if (zblocks < 1) zblocks = 1;
     if (zblocks > 32) zblocks = 32;
@@ -314,13 +337,11 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
     if ((st = record(ev, 1, s))) return st;
     if ((st = record(ev, 2, s))) return st;
   } else {
-    if (!T_dev && cudaMemsetAsync(out_f32, 0, sizeof(float) * T * H, s) != cudaSuccess)
-      return MOE_ERR_CUDA;
     st = launch_route(a, L, s, T_dev);
     if (st) return st;
     if ((st = record(ev, 1, s))) return st;
-    if (launch_programmatic(moe_permute_kernel, dim3(L.blocks), dim3(kRouteThreads), 0, s, pp) !=
-        cudaSuccess)
+    if (launch_programmatic(moe_permute_kernel, dim3(L.blocks, L.permute_split),
+                            dim3(kRouteThreads), 0, s, pp) != cudaSuccess)
       return MOE_ERR_CUDA;
     if ((st = record(ev, 2, s))) return st;
   }
@@ -349,6 +370,8 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   g1.inter_out = ws_ptr<uint8_t>(a, w.inter);
   g1.inter_scale = ws_ptr<float>(a, w.inter_scale);
   g1.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
+  g1.wait_limit_us = wait_limit_us(a->wait_limit_ns);
+  g1.stall = (a->flags & MOE_FLAG_TEST_STALL) != 0 ? 1 : 0;
   if (small) {
     if ((st = launch_gemm_small(kGemm1, tm_b1, tm_a1, g1, dev->sms, s))) return st;
   } else if ((st = launch_gemm(kGemm1, tm_a1, tm_b1, g1, dev->sms, s))) {
@@ -367,7 +390,9 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   g2.row_token = pp.row_token;
   g2.row_weight = pp.row_weight;
   g2.out_f32 = out_f32;
-  const bool fuse_final = small && !T_dev && T <= kFuseFinalMaxTokens;
+  g2.stall = 0;
+  g2.rows_out = det ? ws_ptr<float>(a, w.rows_out) : nullptr;
+  const bool fuse_final = small && !T_dev && !det && T <= kFuseFinalMaxTokens;
   if (fuse_final) {
     g2.final_out = static_cast<__nv_bfloat16*>(a->output);
     g2.final_n8 = T * H / 8;
@@ -385,10 +410,18 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   const int64_t n8 = T * H / 8;
   int blocks = static_cast<int>((n8 + 255) / 256);
   if (blocks > dev->sms * 8) blocks = dev->sms * 8;
-  if (launch_programmatic(moe_finalize_kernel, dim3(blocks), dim3(256), 0, s,
-                          static_cast<const float*>(out_f32), static_cast<__nv_bfloat16*>(a->output),
-                          n8) != cudaSuccess)
-    return MOE_ERR_CUDA;
+  cudaError_t e;
+  if (det)
+    e = launch_programmatic(moe_combine_rows_kernel, dim3(blocks), dim3(256), 0, s,
+                            static_cast<const float*>(g2.rows_out),
+                            static_cast<const int*>(pp.assign_row),
+                            static_cast<__nv_bfloat16*>(a->output), static_cast<int>(T),
+                            static_cast<int>(H), static_cast<int>(a->top_k));
+  else
+    e = launch_programmatic(moe_finalize_kernel, dim3(blocks), dim3(256), 0, s,
+                            static_cast<const float*>(out_f32),
+                            static_cast<__nv_bfloat16*>(a->output), n8);
+  if (e != cudaSuccess) return MOE_ERR_CUDA;
   return record(ev, 5, s);
 }
 
@@ -562,8 +595,12 @@ constexpr size_t kNoAllocScratchBytes = kNoAllocTileOffset + sizeof(int) * (kMax
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch per device.  Host code must not pass the
-// symbol itself to a kernel: on the host it names a host-side stand-in.
+// Device address of g_noalloc_scratch per device, looked up once with the
+// device current and kept for the life of the process (so a first call before
+// any stream capture makes later calls capturable).  The address belongs to
+// the device's primary context: the library is not meant to be used across
+// cudaDeviceReset.  Host code must not pass the symbol itself to a kernel: on
+// the host it names a host-side stand-in.
 unsigned char* g_noalloc_ptr[64];
 std::mutex g_noalloc_mu;
 

@@ -31,9 +31,19 @@ struct CtrlBlock {
   int pad[60];
 };
 
-// Bounded waits give up after this many nanoseconds of %globaltimer.  Normal
-// waits last microseconds; only a broken pipeline reaches the limit.
+// Bounded waits give up after this many nanoseconds of %globaltimer unless the
+// caller set another limit (MoeFwdArgs.wait_limit_ns).  Normal waits last
+// microseconds; only a broken pipeline reaches the limit.  Drains after an
+// abort (letting copies and MMAs already in flight land before shared memory
+// and TMEM are released) always use this default.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+// The limit as the kernels keep it: whole microseconds, at least one.
+__host__ __device__ constexpr unsigned int wait_limit_us(unsigned long long ns) {
+  return ns == 0 ? static_cast<unsigned int>(kWaitLimitNs / 1000)
+         : ns >= 1000ull * 0x7fffffffull ? 0x7fffffffu
+                                         : static_cast<unsigned int>((ns + 999) / 1000);
+}
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
@@ -118,14 +128,15 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 // same sub-partition) nor sleep past the completion (which delays the hand-off).
 constexpr uint32_t kSuspendHintNs = 10000000u;
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity,
+                                              uint32_t hint_ns = kSuspendHintNs) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
@@ -144,19 +155,25 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Suspend-time hint of the retries after a first unsuccessful try_wait: how
+// often a thread in an abnormally long wait looks at the abort flag and the
+// clock.
+constexpr uint32_t kRetryHintNs = 1000000u;
+
 // Wait until the phase with the given parity of `bar` has completed.  Gives up
-// when `*abort` is raised by another warp or after kWaitLimitNs, in which case
-// it raises `*abort`, records MOE_ERR_TIMEOUT with `where` and returns false.
-// Every unsuccessful try_wait has already suspended the thread for up to
-// kSuspendHintNs, so the abort flag and the clock are checked on each round.
+// when `abort[0]` is raised by another warp or when abort[1] microseconds (the
+// CTA's wait limit, kept in the shared word after the flag and read only on
+// this slow path, so that it costs the hot loops no register) have passed
+// since the first try_wait returned; then it raises `abort[0]`, records
+// MOE_ERR_TIMEOUT with `where` and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           CtrlBlock* ctrl, int where) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity, kRetryHintNs)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > 1000ull * static_cast<unsigned int>(abort[1])) {
       *abort = 1;
       report_error(ctrl, MOE_ERR_TIMEOUT, where);
       return false;

@@ -87,15 +87,35 @@ __global__ void __launch_bounds__(kEpThreads) ep_send_plan_kernel(SendPlanParams
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  if (tid < p.world) {
-    int run = 0;
-    for (int b = 0; b < static_cast<int>(gridDim.x); ++b) {
-      int* slot = p.block_cnt + b * p.world + tid;
-      const int v = __ldcg(slot);
-      *slot = run;
-      run += v;
+  // Last block: warp d scans destination d over the blocks; lane l owns the
+  // l-th chunk of blocks, so a lane's loads are independent of each other.
+  const int warp = tid >> 5, lane = tid & 31;
+  const int nb = static_cast<int>(gridDim.x);
+  const int per_lane = (nb + 31) / 32;
+  const int b_lo = min(nb, lane * per_lane), b_hi = min(nb, b_lo + per_lane);
+  if (warp < p.world) {
+    int sum = 0;
+    for (int b = b_lo; b < b_hi; ++b) sum += __ldcg(p.block_cnt + b * p.world + warp);
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
     }
-    p.send_cnt[tid] = run;
+    int run = incl - sum;
+    for (int b0 = b_lo; b0 < b_hi; b0 += 8) {
+      int v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = b0 + i < b_hi ? __ldcg(p.block_cnt + (b0 + i) * p.world + warp) : 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (b0 + i < b_hi) {
+          p.block_cnt[(b0 + i) * p.world + warp] = run;
+          run += v[i];
+        }
+      }
+    }
+    if (lane == 31) p.send_cnt[warp] = incl;
   }
   if (tid == 0) p.ctrl->done = 0u;
 }

@@ -101,9 +101,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* tstart_s = reinterpret_cast<int*>(tmem_slot + 2);
+  uint64_t* never = drain + 1;     // failure-detection tests: completed by nothing
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(never + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);   // [1]: wait limit
+  int* tstart_s = reinterpret_cast<int*>(tmem_slot + 3);
   int* counts_s = tstart_s + kMaxExperts + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -121,7 +122,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty[b], 8);
     }
     mbar_init(drain, kMmaIssuers);
-    *abort_flag = 0;
+    mbar_init(never, 1);
+    abort_flag[0] = 0;
+    abort_flag[1] = static_cast<int>(p.wait_limit_us);
     fence_barrier_init();
   }
   if (warp == 9) {
@@ -169,10 +172,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     producer_done:
-      if (*abort_flag) {
-        for (int s = 0; s < kStages; ++s)
-          if (issued & (1u << s)) drain_wait(&full[s], (issued_phase >> s) & 1u);
-      }
+      // Every load this thread issued lands before the CTA can exit, also
+      // when a consumer gave up on its stage (abort raised at any time).
+      for (int s = 0; s < kStages; ++s)
+        if (issued & (1u << s)) drain_wait(&full[s], (issued_phase >> s) & 1u);
     }
   } else if (warp == 9 || warp == 10) {
     // ------------------------------------------------------------ MMA issuers
@@ -192,6 +195,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t g = 0;
+      if (kMode == kGemm1 && p.stall && me == 0 &&
+          !mbar_wait(never, 0, abort_flag, p.ctrl, 9))
+        goto mma_done;
       for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
         for (int kb = 0; kb < KB; ++kb) {
           bool have_stage = false;
@@ -396,18 +402,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // touches 32 rows x 16 B per instruction.  The weighted values go
         // through the warp's staging tile 16 columns at a time instead, and
         // each red.v4 instruction then adds 64 contiguous bytes to 8 rows.
+        // Deterministic combine: the same values are stored to the row's own
+        // line of rows_out instead, and a gather adds them in a fixed order.
         if (warp_active) {
           const float w = row_valid ? p.row_weight[grow] : 0.f;
           const int tok = row_valid ? p.row_token[grow] : 0;
+          const bool store_rows = p.rows_out != nullptr;
           float* stg = reinterpret_cast<float*>(xpose + warp * kXposeBytesPerWarp);
           float* dst_i[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int rr = 8 * i + (lane >> 2);
             const int t_i = __shfl_sync(0xffffffffu, tok, rr);
+            const int64_t line = store_rows ? static_cast<int64_t>(c.row0) + q * 32 + rr
+                                            : static_cast<int64_t>(t_i);
+            float* base = store_rows ? p.rows_out : p.out_f32;
             dst_i[i] = q * 32 + rr < c.nrows
-                           ? p.out_f32 + static_cast<int64_t>(t_i) * p.hidden + c.n * kTileN +
-                                 128 * h + 4 * (lane & 3)
+                           ? base + line * p.hidden + c.n * kTileN + 128 * h + 4 * (lane & 3)
                            : nullptr;
           }
 #pragma unroll
@@ -424,7 +435,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               const int rr = 8 * i + (lane >> 2);
               const float4 v4 = *reinterpret_cast<const float4*>(
                   reinterpret_cast<const uint8_t*>(stg) + xpose_off(rr, lane & 3));
-              if (dst_i[i]) red_add_v4(dst_i[i] + 16 * ch, v4.x, v4.y, v4.z, v4.w);
+              if (dst_i[i]) {
+                if (store_rows)
+                  *reinterpret_cast<float4*>(dst_i[i] + 16 * ch) = v4;
+                else
+                  red_add_v4(dst_i[i] + 16 * ch, v4.x, v4.y, v4.z, v4.w);
+              }
             }
             __syncwarp();
           }

@@ -182,9 +182,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   uint64_t* tempty = tfull + kSmallBufsMax;
   uint64_t* drain = tempty + kSmallBufsMax;
   uint64_t* ebar = drain + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red_s = reinterpret_cast<float*>(tmem_slot + 2);     // [4][16] amax exchange
+  uint64_t* never = ebar + 1;      // failure-detection tests: completed by nothing
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(never + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);   // [1]: wait limit
+  float* red_s = reinterpret_cast<float*>(tmem_slot + 4);     // [4][16] amax exchange
   int* ustart_s = reinterpret_cast<int*>(red_s + 4 * kSmallN);
   int* counts_s = ustart_s + kMaxExperts + 1;
   int* tstart_s = counts_s + kMaxExperts;
@@ -203,7 +204,9 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     }
     mbar_init(drain, 1);
     mbar_init(ebar, 4);
-    *abort_flag = 0;
+    mbar_init(never, 1);
+    abort_flag[0] = 0;
+    abort_flag[1] = static_cast<int>(p.wait_limit_us);
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -255,7 +258,9 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_units = ustart_s[E];
-  const SegSpace segs = make_seg_space(total_units, KB, kMode == kGemm2);
+  // Split units add partial products, which the deterministic combine's
+  // stored rows cannot take.
+  const SegSpace segs = make_seg_space(total_units, KB, kMode == kGemm2 && p.rows_out == nullptr);
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
@@ -284,10 +289,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
         }
       }
     producer_done:
-      if (*abort_flag) {
-        for (int s = 0; s < S; ++s)
-          if (issued & (1u << s)) drain_wait_s(&full[s], (issued_phase >> s) & 1u);
-      }
+      // Every load this thread issued lands before the CTA can exit, also
+      // when a consumer gave up on its stage (abort raised at any time).
+      for (int s = 0; s < S; ++s)
+        if (issued & (1u << s)) drain_wait_s(&full[s], (issued_phase >> s) & 1u);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
@@ -298,6 +303,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t g = 0;
+      if (kMode == kGemm1 && p.stall && !mbar_wait(never, 0, abort_flag, p.ctrl, 19))
+        goto mma_done;
       for (Seg sg = segs.first(); sg.u >= 0; sg = segs.next(sg)) {
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.ctrl, 12)) goto mma_done;
@@ -541,7 +548,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
             const int64_t row = static_cast<int64_t>(c.row0) + j;
             const int tok = reinterpret_cast<const int*>(sc + kSmallRowOff)[j];
             const float w = sc[kSmallRowOff + kSmallN + j];
-            atomicAdd(p.out_f32 + static_cast<int64_t>(tok) * p.hidden + col, acc[j] * w);
+            if (p.rows_out)   // deterministic combine: the row's own line
+              p.rows_out[row * p.hidden + col] = acc[j] * w;
+            else
+              atomicAdd(p.out_f32 + static_cast<int64_t>(tok) * p.hidden + col, acc[j] * w);
           }
         }
       }

@@ -10,8 +10,8 @@ constexpr int kMaxExperts = 256;       // E_global (and hence E_local) limit
 constexpr int kMaxTopK = 8;
 constexpr int kRouteThreads = 256;     // 8 warps, one token per warp at a time
 constexpr int kMaxTokensPerBlock = 256;
-constexpr int kTinyMaxTokens = 16;
-constexpr int kFuseFinalMaxTokens = 2;   // decode GEMM2 also writes the bf16 output   // batches routed and permuted by one block (moe_route_permute_tiny_kernel)
+constexpr int kTinyMaxTokens = 16;       // batches routed and permuted by one block (moe_route_permute_tiny_kernel)
+constexpr int kFuseFinalMaxTokens = 2;   // decode GEMM2 also writes the bf16 output
 constexpr int kTileM = 128;            // rows (assignments) per GEMM tile
 constexpr int kTileN = 256;            // output columns per GEMM tile
 constexpr int kBlockK = 128;           // K per pipeline stage = scale block
@@ -64,6 +64,7 @@ struct PermuteParams {
   float* a_scale_perm;
   const int* T_dev;    // as RouteParams::T_dev
   float* zero_rows;    // when set, rows t of this [T, H] fp32 buffer are zeroed for every token
+  int* assign_row;     // when set, [T, top_k]: permuted row of every assignment, -1 if not local
 };
 
 // One persistent grouped GEMM launch.  Work units are (expert tile, N tile)
@@ -88,6 +89,10 @@ struct GemmParams {
   float* out_f32;          // GEMM2: [T, H] accumulator
   __nv_bfloat16* final_out;  // decode GEMM2 with few tokens: bf16 output written by the last CTA
   int64_t final_n8;        // T * H / 8
+  float* rows_out;         // GEMM2, deterministic combine: [npad, H] weighted rows, stored
+                           // instead of added into out_f32
+  unsigned int wait_limit_us;         // bound of the bounded waits (wait_limit_us())
+  int stall;               // GEMM1, failure-detection tests: first MMA issuer waits forever
   CtrlBlock* ctrl;
 };
 
@@ -97,6 +102,11 @@ __global__ void moe_route_permute_tiny_kernel(RouteParams rp, PermuteParams pp, 
                                               int64_t acc_n4);
 __global__ void moe_finalize_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out,
                                     int64_t n8);
+// Deterministic combine: out[t] = bf16(sum over k of rows_out[assign_row[t, k]]),
+// k in routing-selection order.
+__global__ void moe_combine_rows_kernel(const float* __restrict__ rows_out,
+                                        const int* __restrict__ assign_row,
+                                        __nv_bfloat16* __restrict__ out, int T, int H, int top_k);
 
 constexpr int kGemm1 = 0;   // gate/up GEMM, SwiGLU + 1x64 FP8 requant epilogue
 constexpr int kGemm2 = 1;   // down GEMM, routing-weighted scatter-add epilogue

@@ -181,23 +181,52 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  // Last block: per-expert exclusive scan over blocks -> bucket base of every
-  // block (token order is block order), per-expert counts, then the prefix sum
-  // of 128-row tiles that places every expert's segment in the permuted
-  // buffers.
+  // Last block: bucket base of every (block, expert) = that expert's count in
+  // all earlier blocks (token order is block order), the per-expert counts,
+  // then the prefix sum of 128-row tiles that places every expert's segment in
+  // the permuted buffers.  Warp w takes the w-th chunk of blocks and lane l the
+  // experts l, l+32, ...: a warp's loads of one block row are coalesced and a
+  // thread's loads do not depend on each other, so the scan costs a few
+  // round trips to L2 instead of one per block.
+  __shared__ int chunk_sum[kRouteThreads / 32][kMaxExperts];
+  constexpr int kWarps = kRouteThreads / 32;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int nb = static_cast<int>(gridDim.x);
+  const int per_chunk = (nb + kWarps - 1) / kWarps;
+  const int b_lo = min(nb, warp * per_chunk), b_hi = min(nb, b_lo + per_chunk);
+  for (int e = lane; e < p.E_local; e += 32) {
+    int sum = 0;
+#pragma unroll 8
+    for (int b = b_lo; b < b_hi; ++b)
+      sum += __ldcg(p.block_base + static_cast<int64_t>(b) * p.E_local + e);
+    chunk_sum[warp][e] = sum;
+  }
+  __syncthreads();
+  for (int e = lane; e < p.E_local; e += 32) {
+    int base = 0;
+    for (int w = 0; w < warp; ++w) base += chunk_sum[w][e];
+    for (int b0 = b_lo; b0 < b_hi; b0 += 8) {
+      int v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = b0 + i < b_hi ? __ldcg(p.block_base + static_cast<int64_t>(b0 + i) * p.E_local + e) : 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (b0 + i < b_hi) {
+          p.block_base[static_cast<int64_t>(b0 + i) * p.E_local + e] = base;
+          base += v[i];
+        }
+      }
+    }
+  }
   int count = 0;
   if (tid < p.E_local) {
-    for (int b = 0; b < static_cast<int>(gridDim.x); ++b) {
-      int* slot = p.block_base + static_cast<int64_t>(b) * p.E_local + tid;
-      const int v = __ldcg(slot);
-      *slot = count;
-      count += v;
-    }
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) count += chunk_sum[w][tid];
     p.counts[tid] = count;
   }
   const int tiles = tid < p.E_local ? (count + kTileM - 1) / kTileM : 0;
   // block-wide exclusive scan of `tiles`
-  const int lane = tid & 31, warp = tid >> 5;
   int incl = tiles;
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
@@ -234,8 +263,11 @@ __device__ __forceinline__ void assign_rows(const PermuteParams& p, const int* i
 }
 
 // Packs the rows of tokens [t0, t1) into the permuted buffers: token, weight
-// and scales per assignment, then the FP8 rows.  All threads of the block.
-__device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* rows_s, int t0, int t1) {
+// and scales per assignment, then the FP8 rows.  All threads of the block;
+// the assignments (and accumulator rows) are shared out over `nsub` blocks
+// with the same tokens, this one being number `sub`.
+__device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* rows_s, int t0, int t1,
+                                          int sub, int nsub) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_assign = (t1 - t0) * p.top_k;
   const int hb = p.H / kBlockK;
@@ -247,8 +279,8 @@ __device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* row
   const int nwarps = blockDim.x >> 5;
   // Few assignments (decode batches): a warp per assignment instead, its lanes
   // over the (at most 64) scale blocks, so that a copy is one round trip.
-  const bool few = n_assign <= 4 * nwarps && hb <= 64;
-  for (int j = warp; few && j < n_assign; j += nwarps) {
+  const bool few = n_assign <= 4 * nwarps * nsub && hb <= 64;
+  for (int j = sub * nwarps + warp; few && j < n_assign; j += nwarps * nsub) {
     const int row = rows_s[j];
     if (row < 0) continue;
     const int t = t0 + j / p.top_k;
@@ -262,7 +294,7 @@ __device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* row
     if (lane < hb) asp[static_cast<int64_t>(lane) * p.npad + row] = v0;
     if (lane + 32 < hb) asp[static_cast<int64_t>(lane + 32) * p.npad + row] = v1;
   }
-  for (int j = tid; !few && j < n_assign; j += blockDim.x) {
+  for (int j = sub * blockDim.x + tid; !few && j < n_assign; j += blockDim.x * nsub) {
     const int row = rows_s[j];
     if (row < 0) continue;
     const int t = t0 + j / p.top_k;
@@ -278,17 +310,23 @@ __device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* row
         if (kb0 + i < hb) asp[static_cast<int64_t>(kb0 + i) * p.npad + row] = v[i];
     }
   }
+  if (p.assign_row) {
+    for (int j = sub * blockDim.x + tid; j < n_assign; j += blockDim.x * nsub)
+      p.assign_row[static_cast<int64_t>(t0) * p.top_k + j] = rows_s[j];
+  }
   if (p.zero_rows) {
     const int64_t n4 = static_cast<int64_t>(t1 - t0) * p.H / 4;
     float4* z = reinterpret_cast<float4*>(p.zero_rows + static_cast<int64_t>(t0) * p.H);
-    for (int64_t i = tid; i < n4; i += blockDim.x) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t i = static_cast<int64_t>(sub) * blockDim.x + tid; i < n4;
+         i += static_cast<int64_t>(blockDim.x) * nsub)
+      z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   // FP8 rows: one warp per assignment, 16-byte vectors, each lane's loads of a
   // row issued before its stores.
   const int vec = p.H / 16;
   const uint8_t* __restrict__ hid = p.hidden;
   uint8_t* __restrict__ ap = p.a_perm;
-  for (int j = warp; j < n_assign; j += nwarps) {
+  for (int j = sub * nwarps + warp; j < n_assign; j += nwarps * nsub) {
     const int row = rows_s[j];
     if (row < 0) continue;
     const int t = t0 + j / p.top_k;
@@ -333,6 +371,9 @@ __device__ __forceinline__ int scan_tiles(int tiles, int* tile_start, int E_loca
 
 }  // namespace
 
+// Grid (route blocks, split): the blocks of one column share the tokens of
+// route block x; each of them assigns all their rows (cheap, warp 0) and packs
+// its share, so that small batches still have enough copies in flight.
 __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParams p) {
   __shared__ int cursor[kMaxExperts];
   __shared__ int rows_s[kMaxTokensPerBlock * kMaxTopK];
@@ -348,7 +389,7 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
   __syncthreads();
   if (warp == 0) assign_rows(p, p.topk_idx, cursor, rows_s, t0, t1, lane);
   __syncthreads();
-  pack_rows(p, rows_s, t0, t1);
+  pack_rows(p, rows_s, t0, t1, blockIdx.y, gridDim.y);
 }
 
 // Decode-sized batches (T <= kTinyMaxTokens, host row count): routing, the
@@ -396,7 +437,7 @@ __global__ void __launch_bounds__(kRouteThreads)
   __syncthreads();
   if (warp == 0) assign_rows(pp, idx_s, cursor, rows_s, 0, rp.T, lane);
   __syncthreads();
-  pack_rows(pp, rows_s, 0, rp.T);
+  pack_rows(pp, rows_s, 0, rp.T, 0, 1);
 }
 
 __global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restrict__ in,
@@ -414,6 +455,33 @@ __global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restri
     r[2] = __floats2bfloat162_rn(b.x, b.y);
     r[3] = __floats2bfloat162_rn(b.z, b.w);
     reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<uint4*>(r);
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    moe_combine_rows_kernel(const float* __restrict__ rows_out, const int* __restrict__ assign_row,
+                            __nv_bfloat16* __restrict__ out, int T, int H, int top_k) {
+  griddep_wait();   // GEMM2's rows are complete
+  const int n8 = H / 8;
+  const int64_t total = static_cast<int64_t>(T) * n8;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const int t = static_cast<int>(i / n8);
+    const int c8 = static_cast<int>(i - static_cast<int64_t>(t) * n8);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < top_k; ++k) {   // routing-selection order, fixed
+      const int r = __ldg(assign_row + static_cast<int64_t>(t) * top_k + k);
+      if (r < 0) continue;
+      const float4* src = reinterpret_cast<const float4*>(rows_out + static_cast<int64_t>(r) * H) + 2 * c8;
+      const float4 a = __ldcs(src), b = __ldcs(src + 1);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    __nv_bfloat162 r2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r2[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<uint4*>(r2);
   }
 }
 

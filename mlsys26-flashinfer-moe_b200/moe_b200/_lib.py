@@ -29,6 +29,9 @@ MOE_BIAS_F32 = 0
 MOE_BIAS_BF16 = 1
 MOE_BIAS_F16 = 2
 
+MOE_FLAG_DETERMINISTIC = 0x1
+MOE_FLAG_TEST_STALL = 0x100
+
 
 class MoeFwdArgs(ctypes.Structure):
     _fields_ = [
@@ -54,6 +57,9 @@ class MoeFwdArgs(ctypes.Structure):
         ("bias_dtype", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("flags", ctypes.c_uint32),
+        ("reserved", ctypes.c_uint32),
+        ("wait_limit_ns", ctypes.c_uint64),
     ]
 
 
@@ -76,6 +82,8 @@ class MoeWorkspaceLayout(ctypes.Structure):
         ("inter", ctypes.c_size_t),
         ("inter_scale", ctypes.c_size_t),
         ("out_f32", ctypes.c_size_t),
+        ("assign_row", ctypes.c_size_t),
+        ("rows_out", ctypes.c_size_t),
     ]
 
 

@@ -59,8 +59,13 @@ def _to_device(t: torch.Tensor, device: torch.device) -> torch.Tensor:
 def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                local_expert_offset: int, routed_scaling_factor: float, output: torch.Tensor,
-               n_group: int = 8, topk_group: int = 4, top_k: int = 8):
+               n_group: int = 8, topk_group: int = 4, top_k: int = 8,
+               deterministic: bool = False):
     """Validate like the reference and fill a ``MoeFwdArgs`` (no workspace yet).
+
+    ``deterministic`` selects the fixed-order combine (``MOE_FLAG_DETERMINISTIC``):
+    bit-identical output from run to run, at the cost of one fp32 row per
+    (token, expert) assignment in the workspace.
 
     Returns ``(args, keepalive, out_dev)``: ``keepalive`` holds the device
     copies the pointers refer to; ``out_dev`` is where the kernel writes (the
@@ -113,6 +118,7 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     a.n_group, a.topk_group, a.top_k = int(n_group), int(topk_group), int(top_k)
     a.routed_scaling_factor = float(routed_scaling_factor)
     a.bias_dtype = _BIAS_DTYPES[routing_bias.dtype]
+    a.flags = _lib.MOE_FLAG_DETERMINISTIC if deterministic else 0
     return a, tensors, out_dev
 
 
@@ -160,18 +166,22 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
         gemm1_weights_scale: torch.Tensor, gemm2_weights: torch.Tensor,
         gemm2_weights_scale: torch.Tensor, local_expert_offset: int,
         routed_scaling_factor: float, output: torch.Tensor, *, n_group: int = 8,
-        topk_group: int = 4, top_k: int = 8, workspace: Optional[torch.Tensor] = None) -> None:
+        topk_group: int = 4, top_k: int = 8, workspace: Optional[torch.Tensor] = None,
+        deterministic: bool = False) -> None:
     """Fused FP8 block-scale DeepSeek-V3 MoE forward (reference ``kernel.py:562``).
 
     Writes the bf16 ``[T, H]`` layer output into ``output``.  Only the experts
     ``[local_expert_offset, local_expert_offset + E_local)`` whose weights are
     passed contribute.  ``workspace`` (uint8 CUDA tensor) may be supplied to
-    avoid the internal per-stream cache.
+    avoid the internal per-stream cache.  ``deterministic=True`` adds each
+    token's expert rows in a fixed order (bit-identical runs) instead of with
+    fp32 atomics as the reference does (kernel.py:246-250).
     """
     args, keep, out_dev = build_args(routing_logits, routing_bias, hidden_states,
                                      hidden_states_scale, gemm1_weights, gemm1_weights_scale,
                                      gemm2_weights, gemm2_weights_scale, local_expert_offset,
-                                     routed_scaling_factor, output, n_group, topk_group, top_k)
+                                     routed_scaling_factor, output, n_group, topk_group, top_k,
+                                     deterministic)
     device = keep[0].device
     if args.T > 0:
         forward_args(args, workspace, device)
@@ -240,4 +250,5 @@ def workspace_views(args: _lib.MoeFwdArgs, workspace: torch.Tensor) -> dict:
         inter=view(lay.inter, npad * i, torch.uint8).view(npad, i),
         inter_scale=view(lay.inter_scale, (i // 64) * npad, torch.float32).view(i // 64, npad),
         out_f32=view(lay.out_f32, t * h, torch.float32).view(t, h),
+        assign_row=view(lay.assign_row, t * k, torch.int32).view(t, k),
     )

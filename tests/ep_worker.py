@@ -76,3 +76,48 @@ def worker(rank, world, port, tokens_per_rank, result_dir):
     np.savez(os.path.join(result_dir, f"rank{rank}.npz"), out=out.float().numpy(), ref=ref,
              sent=tim["rows_sent"], recv=tim["rows_received"])
     dist.destroy_process_group()
+
+
+def failing_worker(rank, world, port, fail_rank, result_dir):
+    """Two expert-parallel steps; rank ``fail_rank`` raises between them.
+
+    The surviving ranks' second step must end with an error (their collective
+    loses its peer, or the process group's short timeout expires) instead of
+    waiting for ever; each rank writes what happened to ``result_dir``.
+    """
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    torch.set_num_threads(1)
+    shape = workloads.tiny_shape(1)
+    wts, tok = rank_inputs(shape, rank, 6)
+    lo, per = ep.expert_range(rank, world, shape.e_global)
+    sl = slice(lo, lo + per)
+
+    def step():
+        out = torch.empty(6, shape.hidden, dtype=torch.bfloat16)
+        ep.ep_forward(tok["routing_logits"], tok["routing_bias"], tok["hidden_states"],
+                      tok["hidden_states_scale"], wts["gemm1_weights"][sl],
+                      wts["gemm1_weights_scale"][sl], wts["gemm2_weights"][sl],
+                      wts["gemm2_weights_scale"][sl], shape.routed_scaling_factor, out,
+                      n_group=shape.n_group, topk_group=shape.topk_group, top_k=shape.top_k,
+                      route_fn=oracle_route, expert_fn=oracle_expert)
+        return out
+
+    step()
+    path = os.path.join(result_dir, f"rank{rank}.txt")
+    if rank == fail_rank:
+        with open(path, "w") as f:
+            f.write("raised")
+        raise RuntimeError(f"injected failure on rank {rank} between steps")
+    t0 = time.time()
+    try:
+        step()
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001 - the test inspects the outcome
+        outcome = f"error {type(e).__name__}"
+    with open(path, "w") as f:
+        f.write(f"{outcome}\n{time.time() - t0:.2f}")
+    os._exit(0)   # the group is broken: no destroy_process_group

@@ -36,3 +36,27 @@ def test_ep_matches_single_process(tmp_path, world, tokens):
         sent_total += int(d["sent"])
         recv_total += int(d["recv"])
     assert sent_total == recv_total          # every dispatched row arrived once
+
+
+def test_rank_failure_between_steps_ends_in_an_error_not_a_hang(tmp_path):
+    """Failure detection on the host: rank 1 raises after the first step; rank
+    0's second step must raise within the process group's timeout (20 s) rather
+    than wait for ever."""
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    procs = [ctx.Process(target=ep_worker.failing_worker, args=(r, 2, port, 1, str(tmp_path)))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+        p.join()
+    assert not alive, "a rank was still waiting after 90 s"
+    assert procs[1].exitcode != 0
+    assert (tmp_path / "rank1.txt").read_text() == "raised"
+    outcome, secs = (tmp_path / "rank0.txt").read_text().split("\n")
+    assert outcome.startswith("error"), outcome
+    assert float(secs) < 60

@@ -241,3 +241,30 @@ def test_tokens_routed_elsewhere_get_zeros(cuda_device):
     none_local = ~((idx >= 0) & (idx < 32)).any(axis=1)
     assert none_local.any()
     assert (bf16_np(out)[none_local] == 0).all()
+
+
+@pytest.mark.parametrize("t,e_local", [(2, 32), (8, 256), (300, 32), (901, 32)])
+def test_deterministic_combine_is_bit_identical(cuda_device, t, e_local):
+    """MOE_FLAG_DETERMINISTIC: three runs give the same bits, and the result
+    agrees with the default (fp32 atomics) path and the oracle.  T=2 and 8 take
+    the decode GEMMs (no split units, no fused bf16 output), 300 and 901 the
+    prefill GEMMs."""
+    from moe_b200 import run
+    inp, shape = dsv3_inputs(t, seed=700 + t, e_local=e_local, local_expert_offset=0)
+    outs = []
+    for _ in range(3):
+        o = torch.empty(t, shape.hidden, dtype=torch.bfloat16, device="cuda")
+        run(*workloads.run_args(inp), o, deterministic=True)
+        outs.append(o)
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16))
+    o_def = torch.empty_like(outs[0])
+    run(*workloads.run_args(inp), o_def)
+    torch.cuda.synchronize()
+    assert (o_def.float() - outs[0].float()).abs().max().item() <= 2e-3
+    toks = np.arange(t) if t <= 8 else np.random.default_rng(t).choice(t, 8, replace=False)
+    ref = oracle_output(inp, shape, tokens=toks)
+    got = bf16_np(outs[0])[toks]
+    assert mo.cosine(got, ref) >= COS
+    np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
