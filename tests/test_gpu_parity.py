@@ -262,7 +262,9 @@ def test_deterministic_combine_is_bit_identical(cuda_device, t, e_local):
     o_def = torch.empty_like(outs[0])
     run(*workloads.run_args(inp), o_def)
     torch.cuda.synchronize()
-    assert (o_def.float() - outs[0].float()).abs().max().item() <= 2e-3
+    # the two paths add the same fp32 terms in different orders: at most one
+    # bf16 rounding step apart (2^-7 relative)
+    torch.testing.assert_close(o_def.float(), outs[0].float(), rtol=2.0 ** -7, atol=1e-4)
     toks = np.arange(t) if t <= 8 else np.random.default_rng(t).choice(t, 8, replace=False)
     ref = oracle_output(inp, shape, tokens=toks)
     got = bf16_np(outs[0])[toks]
