@@ -74,7 +74,13 @@ def parse():
                          "same-density case used for ncu captures")
     ap.add_argument("--zipf", type=float, default=None,
                     help="headline run with Zipf(s)-skewed routing (config 3) instead")
+    ap.add_argument("--concentrate", action="store_true",
+                    help="router bias +10 on the local experts, so every token's experts are "
+                         "local: T=1 with --e-local 8 does the work of a 256-expert decode step "
+                         "with 0.35 GB of weights resident (for ncu captures)")
     ap.add_argument("--flashinfer-contest", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--build-flashinfer", action="store_true",
+                    help="compile FlashInfer's MoE launcher (the comparator) and exit")
     return ap.parse_args()
 
 
@@ -353,13 +359,17 @@ def run_ours(a):
     torch.cuda.set_device(0)
     peaks, peak_kind = load_peaks()
     t = a.tokens or 8192
-    full = workloads.dsv3_shape(t)
-    weights = workloads.make_inputs(full, seed=0, device="cuda")   # tokens of seed 0 + all weights
+    full = workloads.dsv3_shape(t, e_local=256 if not a.no_extras else a.e_local)
+    # tokens of seed 0 + the weights (all 256 experts unless only the headline runs)
+    weights = workloads.make_inputs(full, seed=0, device="cuda")
     shape = workloads.dsv3_shape(t, e_local=a.e_local)
     if a.zipf is None:
         inp = {k: (v[:shape.e_local] if k in WEIGHT_KEYS else v) for k, v in weights.items()}
     else:
         inp = layer_inputs(weights, shape, seed=0, zipf=a.zipf)
+    if a.concentrate:
+        inp["routing_bias"] = inp["routing_bias"].clone()
+        inp["routing_bias"][:shape.e_local] += 10.0
     runner = Runner(torch, shape, inp)
     clocks = ClockSampler(torch.cuda.current_device())
     # timed region: K plain forwards
@@ -401,6 +411,8 @@ def run_ours(a):
     }
     cfg_name = "config 3, Zipf routing" if a.zipf is not None else \
         ("config 2" if shape.e_local == 256 else "same-density subset")
+    if a.concentrate:
+        cfg_name = "routing concentrated on the local experts, profiling case"
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": 1,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 4),
@@ -649,10 +661,36 @@ def contest_weights():
     return workloads.make_inputs(workloads.dsv3_shape(8192, e_local=32), seed=0, device="cuda")
 
 
+# FlashInfer JIT-compiles the launcher of its MoE kernels on first use (minutes
+# of nvcc).  The build is made once in this directory (git-ignored) and carried
+# to the GPU box with the repository; the closed kernels themselves come from
+# the installed flashinfer-cubin package.
+FLASHINFER_JIT = os.path.join(REPO, "baseline", "_flashinfer_jit")
+
+
+def flashinfer_env():
+    os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", FLASHINFER_JIT)
+    os.environ.setdefault("FLASHINFER_CUDA_ARCH_LIST", "10.0a")
+
+
+def flashinfer_jit_ready():
+    import glob
+    return bool(glob.glob(os.path.join(FLASHINFER_JIT, ".cache", "flashinfer", "*", "100a",
+                                       "cached_ops", "fused_moe_trtllm_sm100", "*.so")))
+
+
+def build_flashinfer():
+    """Compile FlashInfer's MoE launcher into FLASHINFER_JIT (no GPU needed)."""
+    flashinfer_env()
+    from flashinfer.fused_moe.core import gen_trtllm_gen_fused_moe_sm100_module
+    gen_trtllm_gen_fused_moe_sm100_module().build(verbose=False)
+
+
 def run_flashinfer_contest():
     """Child process of the contest sweep: FlashInfer's kernel on the contest
     inputs, timed like ours, plus the cosine of its output against ours.
     Prints one JSON dict {n: {...}}; an exception is reported as a string."""
+    flashinfer_env()
     import torch
     torch.cuda.set_device(0)
     weights = contest_weights()
@@ -686,11 +724,14 @@ def run_flashinfer_contest():
 
 def flashinfer_contest_child():
     import subprocess
+    if not flashinfer_jit_ready():
+        return None, ("FlashInfer's MoE launcher is not built in baseline/_flashinfer_jit "
+                      "(python bench.py --build-flashinfer, no GPU needed)")
     try:
         p = subprocess.run([sys.executable, os.path.abspath(__file__), "--flashinfer-contest"],
-                           capture_output=True, text=True, timeout=600)
+                           capture_output=True, text=True, timeout=300)
     except subprocess.TimeoutExpired:
-        return None, "timed out after 600 s"
+        return None, "timed out after 300 s"
     for line in p.stdout.splitlines():
         if line.startswith("FLASHINFER_JSON "):
             return json.loads(line[len("FLASHINFER_JSON "):]), None
@@ -982,7 +1023,9 @@ def run_reference(a):
 
 def main():
     a = parse()
-    if a.flashinfer_contest:
+    if a.build_flashinfer:
+        build_flashinfer()
+    elif a.flashinfer_contest:
         run_flashinfer_contest()
     elif a.impl == "reference":
         run_reference(a)

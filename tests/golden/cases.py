@@ -50,3 +50,40 @@ def case_inputs(name: str):
             inp[k] = inp[k][lo:lo + el].contiguous()
     inp["local_expert_offset"] = shape.local_expert_offset
     return inp, shape, spec
+
+
+# The contest shape (FlashInfer-Bench definition, kernel.py:577-588): DeepSeek-V3
+# H=7168, I=2048, experts 0..31 of 256 local.  One set of 32 experts' weights
+# (CPU generator, seed CONTEST_WEIGHT_SEED) is shared by the cases; each case
+# draws its own tokens.  The fixtures keep routing and dispatch in full and a
+# sample of intermediate rows and output tokens (make_golden.py --contest).
+CONTEST_WEIGHT_SEED = 50
+CONTEST_CASES = {
+    "dsv3_e32_t7": dict(t=7, seed=51),
+    "dsv3_e32_t80": dict(t=80, seed=52),
+    "dsv3_e32_t901": dict(t=901, seed=53),
+}
+WEIGHT_KEYS = ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")
+_contest_weights = {}
+
+
+def contest_weights():
+    if not _contest_weights:
+        w = workloads.make_inputs(workloads.dsv3_shape(1, e_local=32), seed=CONTEST_WEIGHT_SEED,
+                                  device="cpu")
+        _contest_weights.update({k: w[k] for k in WEIGHT_KEYS})
+    return _contest_weights
+
+
+def contest_case_inputs(name: str):
+    spec = CONTEST_CASES[name]
+    shape = workloads.dsv3_shape(spec["t"], e_local=32, local_expert_offset=0)
+    inp = workloads.make_inputs(shape, seed=spec["seed"], device="cpu", weights=False)
+    inp.update(contest_weights())
+    return inp, shape, spec
+
+
+def contest_sample_tokens(t: int):
+    """Tokens whose output rows a contest fixture keeps."""
+    import numpy as np
+    return np.arange(t) if t <= 16 else np.sort(np.random.default_rng(t).choice(t, 16, replace=False))

@@ -24,8 +24,11 @@ mantissa carry corrupt the exponent (``triton/runtime/interpreter.py``
 even conversion, which is what the compiled GPU kernel does; everything else in
 the interpreter is left as is.
 
-Usage: ``python tests/golden/make_golden.py --ref DIR`` (DIR: a checkout of the
-reference; the committed .npz files are what the tests read).
+Usage: ``python tests/golden/make_golden.py --ref DIR [--contest]`` (DIR: a
+checkout of the reference; the committed .npz files are what the tests read).
+``--contest`` makes the DeepSeek-V3 contest-shape cases (H=7168, I=2048, 32
+of 256 experts local), which keep routing and dispatch in full and a sample
+of intermediate rows and output tokens.
 """
 from __future__ import annotations
 
@@ -165,17 +168,47 @@ def make_case(ref, name: str):
           meta["digest"][:16])
 
 
+def make_contest_case(ref, name: str, inter_rows: int = 24):
+    """A contest-shape case (DeepSeek-V3, 32 of 256 experts local).  Routing and
+    dispatch are kept in full; the intermediate for the first ``inter_rows``
+    rows in bucket order and the output for ``cases.contest_sample_tokens``."""
+    import time
+    inp, shape, spec = cases.contest_case_inputs(name)
+    t0 = time.time()
+    res = drive_reference(ref, inp, shape)
+    n = int(res["starts"][-1])
+    k = min(n, inter_rows)
+    toks = cases.contest_sample_tokens(shape.t)
+    keep = dict(topk_idx=res["topk_idx"], topk_weights=res["topk_weights"], counts=res["counts"],
+                starts=res["starts"], sorted_tokens=res["sorted_tokens"],
+                sorted_weights=res["sorted_weights"], tile_expert=res["tile_expert"],
+                tile_local_m=res["tile_local_m"], inter_rows=np.arange(k),
+                gemm1_out=res["gemm1_out"][:k], gemm1_scale=res["gemm1_scale"][:, :k],
+                sample_tokens=toks, output_bf16=res["output_bf16"][toks])
+    meta = dict(name=name, seed=spec["seed"], weight_seed=cases.CONTEST_WEIGHT_SEED,
+                digest=workloads.tensor_digest(inp),
+                **{kk: v for kk, v in shape.__dict__.items()},
+                generator="tests/golden/cases.py contest_case_inputs",
+                reference="kernel.py kernels under TRITON_INTERPRET=1 (fp8 cast fixed)")
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), meta=np.array(repr(meta)), **keep)
+    print(name, "tokens", shape.t, "local assignments", n, "digest", meta["digest"][:16],
+          f"{time.time() - t0:.0f} s")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="checkout of the reference solution (read-only)")
     ap.add_argument("--case", default=None)
+    ap.add_argument("--contest", action="store_true",
+                    help="the DeepSeek-V3 contest-shape cases (cases.CONTEST_CASES)")
     a = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
     ref = load_reference(a.ref)
-    for name in cases.CASES:
+    names = cases.CONTEST_CASES if a.contest else cases.CASES
+    for name in names:
         if a.case and a.case != name:
             continue
-        make_case(ref, name)
+        (make_contest_case if a.contest else make_case)(ref, name)
 
 
 if __name__ == "__main__":

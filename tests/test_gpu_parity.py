@@ -13,6 +13,7 @@ Bars:
   ~0.08, beyond atol 1e-2, so the bar is the requantising oracle's own error.
 """
 import ast
+import os
 
 import numpy as np
 import pytest
@@ -270,3 +271,102 @@ def test_deterministic_combine_is_bit_identical(cuda_device, t, e_local):
     got = bf16_np(outs[0])[toks]
     assert mo.cosine(got, ref) >= COS
     np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
+
+
+# ---------------------------------------------------------------- contest-shape fixtures
+
+CONTEST_FIXTURES = [n for n in cases.CONTEST_CASES if os.path.exists(f"{cases.HERE}/{n}.npz")]
+
+
+@pytest.mark.parametrize("name", CONTEST_FIXTURES)
+def test_contest_fixture_from_reference_kernels(cuda_device, name):
+    """DeepSeek-V3 contest shape (H=7168, I=2048, experts 0..31 of 256) against
+    the reference's own kernels (Triton interpreter, tests/golden/make_golden.py
+    --contest): routing and the per-expert token lists bit-exact, the sampled
+    FP8 intermediate rows and scales, and the sampled output tokens within the
+    tests' tolerance."""
+    g = np.load(f"{cases.HERE}/{name}.npz")
+    meta = ast.literal_eval(str(g["meta"]))
+    inp, shape, _ = cases.contest_case_inputs(name)
+    assert workloads.tensor_digest(inp) == meta["digest"]
+    out, views, _ = run_cuda(to_cuda(inp), shape)
+    np.testing.assert_array_equal(views["topk_idx"].cpu().numpy(), g["topk_idx"])
+    np.testing.assert_allclose(views["topk_weights"].cpu().numpy(), g["topk_weights"], rtol=2e-6)
+    np.testing.assert_array_equal(views["counts"].cpu().numpy(), g["counts"])
+    tstart = views["tile_start"].cpu().numpy()
+    row_tok = views["row_token"].cpu().numpy()
+    st, stok = g["starts"], g["sorted_tokens"]
+    for e in range(shape.e_local):
+        ours = row_tok[128 * tstart[e]: 128 * tstart[e] + g["counts"][e]]
+        np.testing.assert_array_equal(ours, np.sort(stok[st[e]:st[e + 1]]))
+    # sampled intermediate rows: fixture row p (bucket position in the
+    # reference's order) -> our row of the same (expert, token)
+    inter = views["inter"].cpu().numpy()
+    isc = views["inter_scale"].cpu().numpy()
+    same = total = 0
+    for j, p in enumerate(g["inter_rows"]):
+        e = int(np.searchsorted(st, p, side="right") - 1)
+        tok = stok[p]
+        ours_row = 128 * tstart[e] + int(np.searchsorted(np.sort(stok[st[e]:st[e + 1]]), tok))
+        np.testing.assert_allclose(isc[:, ours_row], g["gemm1_scale"][:, j], rtol=1e-5)
+        same += int((inter[ours_row] == g["gemm1_out"][j]).sum())
+        total += inter.shape[1]
+    assert total == 0 or same / total > 0.999
+    toks = g["sample_tokens"]
+    got = bf16_np(out)[toks]
+    ref = mo.bf16_to_f32(g["output_bf16"])
+    np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
+    assert mo.cosine(got, ref) >= COS
+
+
+def torch_fp32_layer(inp, shape, topk_idx, topk_w):
+    """The layer in fp32 PyTorch on the GPU for every token, given the routing:
+    dequantised operands, fp32 GEMMs (TF32 off), SwiGLU, the reference's 1x64
+    FP8 requant of the intermediate (kernel.py:128-135, torch's RNE cast) and
+    the routing-weighted sum (kernel.py:236-250)."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    t, h, i = shape.t, shape.hidden, shape.inter
+    a = inp["hidden_states"].float().view(t, h // 128, 128) * \
+        inp["hidden_states_scale"].t().reshape(t, h // 128, 1)
+    a = a.view(t, h)
+    out = torch.zeros(t, h, dtype=torch.float32, device="cuda")
+    loc = topk_idx.long() - shape.local_expert_offset
+    for e in range(shape.e_local):
+        sel = (loc == e).nonzero()
+        if sel.numel() == 0:
+            continue
+        tok, kk = sel[:, 0], sel[:, 1]
+        w1 = inp["gemm1_weights"][e].float().view(2 * i // 128, 128, h // 128, 128) * \
+            inp["gemm1_weights_scale"][e].view(2 * i // 128, 1, h // 128, 1)
+        g = a[tok] @ w1.view(2 * i, h).t()
+        c = torch.nn.functional.silu(g[:, i:]) * g[:, :i]
+        cb = c.view(-1, i // 64, 64)
+        sc = torch.clamp(cb.abs().amax(dim=2, keepdim=True) / 448.0, min=1e-12)
+        cq = (cb / sc).to(torch.float8_e4m3fn).float() * sc
+        w2 = inp["gemm2_weights"][e].float().view(h // 128, 128, i // 128, 128) * \
+            inp["gemm2_weights_scale"][e].view(h // 128, 1, i // 128, 1)
+        d = cq.view(-1, i) @ w2.view(h, i).t()
+        out.index_add_(0, tok, d * topk_w[tok, kk].unsqueeze(1))
+    return out
+
+
+def test_prefill_full_output_against_torch_fp32(cuda_device):
+    """Every output element of a T=2048, 256-expert prefill (all 56 K blocks of
+    GEMM1, the persistent multi-wave schedule) against the fp32 PyTorch layer;
+    that reference is itself checked against the numpy oracle on sampled
+    tokens."""
+    inp, shape = dsv3_inputs(2048, seed=17)
+    out, views, _ = run_cuda(inp, shape)
+    check_routing_and_dispatch(views, inp, shape)
+    ref = torch_fp32_layer(inp, shape, views["topk_idx"], views["topk_weights"])
+    toks = np.random.default_rng(17).choice(2048, 4, replace=False)
+    ora = oracle_output(inp, shape, tokens=toks)
+    assert mo.cosine(ref[toks].cpu().numpy(), ora) >= 0.99999
+    np.testing.assert_allclose(ref[toks].cpu().numpy(), ora, atol=1e-2, rtol=2e-2)
+    got = out.float()
+    torch.testing.assert_close(got, ref, atol=ATOL, rtol=RTOL)
+    cos = torch.dot(got.flatten(), ref.flatten()) / (got.norm() * ref.norm())
+    assert cos.item() >= COS
+    # per-token cosine, so that no single token hides in the global figure
+    tc = (got * ref).sum(1) / (got.norm(dim=1) * ref.norm(dim=1) + 1e-30)
+    assert tc.min().item() >= 0.999

@@ -5,9 +5,11 @@ under the Triton interpreter (``tests/golden/make_golden.py``).  These tests pin
 the oracle that the GPU parity tests rely on.  CPU only.
 """
 import ast
+import os
 
 import numpy as np
 import pytest
+import torch
 
 import cases
 import moe_oracle as mo
@@ -148,3 +150,53 @@ def test_routing_bias_only_selects():
     # the 4 lowest unchosen experts of those groups.
     assert set(idx[0][:4]) == {3, 40, 77, 100}
     np.testing.assert_allclose(w.sum(), 1.0, rtol=1e-6)
+
+
+# ---------------------------------------------------------------- contest shape
+
+CONTEST_NAMES = [n for n in cases.CONTEST_CASES if os.path.exists(f"{cases.HERE}/{n}.npz")]
+_expert_cache = {}
+
+
+def load_contest(name):
+    g = np.load(f"{cases.HERE}/{name}.npz")
+    meta = ast.literal_eval(str(g["meta"]))
+    inp, shape, _ = cases.contest_case_inputs(name)
+    return g, meta, inp, shape
+
+
+def contest_expert(inp, e):
+    if e not in _expert_cache:
+        _expert_cache[e] = tuple(inp[k][e].view(torch.uint8).numpy() if inp[k].dtype ==
+                                 torch.float8_e4m3fn else inp[k][e].numpy()
+                                 for k in cases.WEIGHT_KEYS)
+    return _expert_cache[e]
+
+
+@pytest.mark.parametrize("name", CONTEST_NAMES)
+def test_contest_routing_dispatch_and_output(name):
+    """DeepSeek-V3 contest shape (H=7168, I=2048, 32 of 256 experts): the
+    oracle's routing and dispatch equal the reference kernels' bit for bit, and
+    its output matches theirs on the fixture's first sampled tokens."""
+    g, meta, inp, s = load_contest(name)
+    assert workloads.tensor_digest(inp) == meta["digest"]
+    ni = {k: v for k, v in mo.to_numpy_inputs({k: v for k, v in inp.items()
+                                               if k not in cases.WEIGHT_KEYS}).items()}
+    idx, w = mo.route(ni["routing_logits"], ni["routing_bias"], s.n_group, s.topk_group, s.top_k,
+                      s.routed_scaling_factor)
+    np.testing.assert_array_equal(idx, g["topk_idx"])
+    np.testing.assert_allclose(w, g["topk_weights"], rtol=2e-6, atol=0)
+    counts, starts, tok, wt = mo.dispatch(idx, w, s.local_expert_offset, s.e_local)
+    np.testing.assert_array_equal(counts, g["counts"])
+    np.testing.assert_array_equal(starts, g["starts"])
+    for e in range(s.e_local):
+        a, b = starts[e], starts[e + 1]
+        np.testing.assert_array_equal(tok[a:b], np.sort(g["sorted_tokens"][a:b]))
+    toks = g["sample_tokens"][:4]
+    hi = dict(ni, local_expert_offset=0, routed_scaling_factor=s.routed_scaling_factor,
+              e_local=s.e_local)
+    ref = mo.moe_forward(hi, s.n_group, s.topk_group, s.top_k, tokens=toks,
+                         get_expert=lambda e: contest_expert(inp, e))
+    got = mo.bf16_to_f32(g["output_bf16"][:4])
+    np.testing.assert_allclose(ref, got, atol=1e-2, rtol=2e-2)
+    assert mo.cosine(ref, got) >= 0.9999
