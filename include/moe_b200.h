@@ -140,7 +140,7 @@ int moe_fp8_forward(const MoeFwdArgs* a, void* stream);
  * created) on `stream` at the stage boundaries, for per-kernel timing:
  *   events[0] start, [1] after routing (+ accumulator zeroing), [2] after the
  *   permute/pack, [3] after GEMM1, [4] after GEMM2, [5] after the bf16 cast.
- * For T <= 16 routing and packing are one kernel ([1] and [2] are recorded
+ * For T <= 4 routing and packing are one kernel ([1] and [2] are recorded
  * together after it); for T <= 2 GEMM2 also writes the bf16 output ([4] and [5]
  * together).  Events between kernels can reduce the overlap that programmatic
  * dependent launch gives an unprofiled forward.

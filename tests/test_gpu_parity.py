@@ -96,11 +96,12 @@ def dsv3_inputs(t, seed, **kw):
     return inp, shape
 
 
-@pytest.mark.parametrize("t,offset", [(1, 0), (2, 128), (7, 96), (80, 224), (901, 32)])
+@pytest.mark.parametrize("t,offset", [(1, 0), (2, 128), (4, 64), (7, 96), (80, 224), (901, 32)])
 def test_contest_shape_32_local_experts(cuda_device, t, offset):
     """The FlashInfer-Bench definition: 32 local experts of 256 (kernel.py:581).
-    T <= 2 exercises the GEMM2 that writes the bf16 output itself, T <= 16 the
-    one-launch route/pack, T=80 and 901 the separate route and permute kernels."""
+    T <= 2 exercises the GEMM2 that writes the bf16 output itself, T <= 4 the
+    one-launch route/pack, T=7, 80 and 901 the separate route and permute
+    kernels."""
     inp, shape = dsv3_inputs(t, seed=10 + t, e_local=32, local_expert_offset=offset)
     out, views, _ = run_cuda(inp, shape)
     check_routing_and_dispatch(views, inp, shape)
