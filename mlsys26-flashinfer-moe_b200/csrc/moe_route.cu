@@ -35,6 +35,13 @@ __device__ __forceinline__ float sigmoid_f32(float x) {
   return static_cast<float>(1.0 / (1.0 + exp(-static_cast<double>(x))));
 }
 
+// Unsigned key with the order of the float: flip all bits of negatives, the
+// sign bit of the rest (-inf is the smallest key).
+__device__ __forceinline__ unsigned ordered_key(float v) {
+  const unsigned b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 // One token on one warp.  Lane l holds experts [l*EPL, (l+1)*EPL); a group of
 // G experts spans LPG = G/EPL consecutive lanes.
 template <int EPL>
@@ -81,37 +88,39 @@ __device__ __forceinline__ void route_one_token(const RouteParams& p, int t, int
   float cand[EPL];
 #pragma unroll
   for (int j = 0; j < EPL; ++j) cand[j] = keep ? sb[j] : -INFINITY;
-  // --- top_k experts by sb, ties to the lowest expert id (522-534)
+  // --- top_k experts by sb, ties to the lowest expert id (522-534).  Each
+  // round: the lane's best candidate (first of equal values, so its lowest
+  // expert), the warp maximum of an order-preserving integer key in one
+  // redux, and the lowest lane holding it -- lane l owns experts
+  // [l*EPL, (l+1)*EPL), so that lane's candidate is the lowest expert id
+  // among the equal maxima, as in the reference's max-and-mask.
   int my_idx = 0;
   float my_s = 0.f;
   for (int k = 0; k < p.top_k; ++k) {
     float bv = -INFINITY;
-    int bi = 0x7fffffff;
+    int bj = 0;
 #pragma unroll
     for (int j = 0; j < EPL; ++j) {
       if (cand[j] > bv) {
         bv = cand[j];
-        bi = e0 + j;
+        bj = j;
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(full, bv, off);
-      const int oi = __shfl_xor_sync(full, bi, off);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
+    const unsigned key = ordered_key(bv);
+    const unsigned kmax = __reduce_max_sync(full, key);
+    const int src = __ffs(__ballot_sync(full, key == kmax)) - 1;
     float sv = 0.f;
+    if (lane == src) {
 #pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      if (e0 + j == bi) {
-        sv = s[j];
-        cand[j] = -INFINITY;
+      for (int j = 0; j < EPL; ++j) {
+        if (j == bj) {
+          sv = s[j];
+          cand[j] = -INFINITY;
+        }
       }
     }
-    sv = __shfl_sync(full, sv, min(bi / EPL, 31));
+    const int bi = __shfl_sync(full, e0 + bj, src);
+    sv = __shfl_sync(full, sv, src);
     if (lane == k) {
       my_idx = bi;
       my_s = sv;

@@ -380,3 +380,31 @@ def test_prefill_full_output_against_torch_fp32(cuda_device):
     # per-token cosine, so that no single token hides in the global figure
     tc = (got * ref).sum(1) / (got.norm(dim=1) * ref.norm(dim=1) + 1e-30)
     assert tc.min().item() >= 0.999
+
+
+def test_routing_exact_ties_match_the_oracle(cuda_device):
+    """Routing with exact ties, bit-exact against the oracle (lowest group and
+    expert id win, kernel.py:497-499, 524-525): all-equal scores; a few values
+    repeated across groups and inside a lane's experts; a bias that makes every
+    group's top-2 sum equal; and one-hot scores that tie the rest."""
+    e, t = 256, 6
+    rng = np.random.default_rng(5)
+    logits = np.zeros((t, e), np.float32)
+    logits[1] = rng.choice(np.array([-1.0, 0.0, 0.5, 2.0], np.float32), e)
+    logits[2] = np.repeat(np.arange(32, dtype=np.float32) * 0.25, 8)[::-1]
+    logits[3] = np.tile(np.array([0.0, 1.0, 1.0, 0.0, 2.0, 2.0, 2.0, 0.0], np.float32), 32)
+    logits[4, ::37] = 3.0
+    logits[5] = rng.standard_normal(e).astype(np.float32).round(1)
+    bias = np.zeros(e, np.float32)
+    bias[::32] = 0.5           # every group gets the same head
+    full = workloads.make_inputs(workloads.dsv3_shape(t), seed=9, device="cuda")
+    for tt in (t, 3):          # the routing kernel, and the one-block route+pack
+        shape = workloads.dsv3_shape(tt)
+        inp = dict(full)
+        inp["routing_logits"] = torch.from_numpy(logits[:tt]).cuda()
+        inp["hidden_states"] = full["hidden_states"][:tt].contiguous()
+        inp["hidden_states_scale"] = full["hidden_states_scale"][:, :tt].contiguous()
+        for b in (np.zeros(e, np.float32), bias):
+            inp["routing_bias"] = torch.from_numpy(b).cuda()
+            _, views, _ = run_cuda(inp, shape)
+            check_routing_and_dispatch(views, inp, shape)
