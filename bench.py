@@ -718,8 +718,12 @@ def run_flashinfer_contest():
             r.forward()
             torch.cuda.synchronize()
             a_, b_ = r.out.float().flatten(), fo.float().flatten()
-            cos = float(torch.dot(a_, b_) / (a_.norm() * b_.norm() + 1e-30))
-            res[str(n)] = {"ms": round(fms, 4), "cos_vs_ours": round(cos, 6)}
+            if a_.norm() == 0 and b_.norm() == 0:
+                cos = 1.0   # no token routed to a local expert: both outputs are zero
+            else:
+                cos = float(torch.dot(a_, b_) / (a_.norm() * b_.norm() + 1e-30))
+            res[str(n)] = {"ms": round(fms, 4), "cos_vs_ours": round(cos, 6),
+                           "max_abs_diff_vs_ours": round(float((a_ - b_).abs().max()), 5)}
             del r
         except Exception as exc:  # noqa: BLE001 - reported to the parent
             res[str(n)] = f"{type(exc).__name__}: {str(exc)[:300]}"
