@@ -44,18 +44,26 @@ __device__ __forceinline__ unsigned ordered_key(float v) {
 
 // One token on one warp.  Lane l holds experts [l*EPL, (l+1)*EPL); a group of
 // G experts spans LPG = G/EPL consecutive lanes.
+// Lane's logits of token t (zeros past E).
+template <int EPL>
+__device__ __forceinline__ void load_logits(const RouteParams& p, int t, int lane, float (&x)[EPL]) {
+  const int e0 = lane * EPL;
+  const float* row = p.logits + static_cast<int64_t>(t) * p.E;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) x[j] = e0 < p.E ? __ldg(row + e0 + j) : 0.f;
+}
+
 template <int EPL>
 __device__ __forceinline__ void route_one_token(const RouteParams& p, int t, int lane,
-                                                const float (&bias)[EPL], int* hist_s, int* idx_s) {
+                                                const float (&x)[EPL], const float (&bias)[EPL],
+                                                int* hist_s, int* idx_s) {
   const unsigned full = 0xffffffffu;
   const int e0 = lane * EPL;
   const bool active = e0 < p.E;
   float s[EPL], sb[EPL];
-  const float* row = p.logits + static_cast<int64_t>(t) * p.E;
 #pragma unroll
   for (int j = 0; j < EPL; ++j) {
-    const float x = active ? __ldg(row + e0 + j) : 0.f;
-    s[j] = sigmoid_f32(x);
+    s[j] = sigmoid_f32(x[j]);
     sb[j] = active ? s[j] + bias[j] : -INFINITY;
   }
   // --- group score: sum of the two largest sb in the group (kernel.py:479-488)
@@ -161,8 +169,20 @@ __device__ __forceinline__ void route_block_tokens(const RouteParams& p, int* hi
   const int T = p.T_dev ? min(p.T, *p.T_dev) : p.T;
   const int t0 = blockIdx.x * p.tokens_per_block;
   const int t1 = min(T, t0 + p.tokens_per_block);
-  for (int t = t0 + warp; t < t1; t += kRouteThreads / 32)
-    route_one_token<EPL>(p, t, lane, bias, hist_s, idx_s);
+  // A warp's tokens are t0 + warp + 8i; their logits are loaded kBatch at a
+  // time before any of them is routed, so the warp waits for DRAM once per
+  // batch instead of once per token.
+  constexpr int kWarps = kRouteThreads / 32;
+  constexpr int kBatch = EPL >= 8 ? 4 : 8;
+  for (int tb = t0 + warp; tb < t1; tb += kWarps * kBatch) {
+    float x[kBatch][EPL];
+#pragma unroll
+    for (int c = 0; c < kBatch; ++c)
+      if (tb + kWarps * c < t1) load_logits<EPL>(p, tb + kWarps * c, lane, x[c]);
+#pragma unroll
+    for (int c = 0; c < kBatch; ++c)
+      if (tb + kWarps * c < t1) route_one_token<EPL>(p, tb + kWarps * c, lane, x[c], bias, hist_s, idx_s);
+  }
 }
 
 }  // namespace
