@@ -95,6 +95,11 @@ typedef struct MoeFwdArgs {
   uint32_t flags;              /* MOE_FLAG_*; 0 = reference behaviour */
   uint32_t reserved;           /* must be 0 */
   uint64_t wait_limit_ns;      /* bound of every device-side wait; 0 = 2 s */
+  /* Optional: the down-projection weights prepared once by
+   * moe_fp8_prepare_gemm2_bf16, [E_local, H, I] bf16.  When set, batches on the
+   * prefill path run GEMM2 on bf16 operands without block-scale promotion
+   * (GEMM1 then writes the dequantised intermediate); NULL = FP8 path. */
+  const void* gemm2_weights_bf16;
 } MoeFwdArgs;
 
 /* Offsets (bytes from the workspace base) of the per-stage buffers a forward
@@ -120,6 +125,7 @@ typedef struct MoeWorkspaceLayout {
   size_t out_f32;          /* [T, H] fp32        scatter-add accumulator */
   size_t assign_row;       /* [T, top_k] int32   permuted row of each assignment (-1: not local) */
   size_t rows_out;         /* [npad, H] fp32     weighted GEMM2 rows (MOE_FLAG_DETERMINISTIC only) */
+  size_t inter_bf16;       /* [npad, I] bf16     dequantised intermediate (gemm2_weights_bf16 only) */
 } MoeWorkspaceLayout;
 
 /* Workspace bytes needed for the shape in `a` (pointers are not read).
@@ -188,6 +194,17 @@ int moe_fp8_route_noalloc(const float* routing_logits, const void* routing_bias,
                           int64_t local_expert_offset, float routed_scaling_factor,
                           int32_t* topk_idx, float* topk_weights, int32_t* expert_counts,
                           void* stream);
+
+/* One-time relayout of the down-projection weights for the bf16 GEMM2:
+ * out[e, h, i] = bf16(float(W2[e, h, i]) * W2_scale[e, h/128, i/128]), the
+ * reference's dequantised weight (kernel.py:224-234) rounded once to bf16.
+ * w2 [E_local, H, I] e4m3, w2_scale [E_local, H/128, I/128] fp32, out
+ * [E_local, H, I] bf16 (twice the bytes of w2).  Pass `out` as
+ * MoeFwdArgs.gemm2_weights_bf16 to later forwards with the same weights.  No
+ * counterpart in the reference (SURVEY's one-time weight relayout).  Asynchronous
+ * on `stream`, no allocation; H, I multiples of 128, pointers 16-byte aligned. */
+int moe_fp8_prepare_gemm2_bf16(const void* w2, const float* w2_scale, int64_t E_local, int64_t H,
+                               int64_t I, void* out, void* stream);
 
 /* bf16 -> FP8 e4m3 quantisation of activations with one fp32 scale per token
  * and 128 columns: x [T, H] bf16 (row-major) -> q [T, H] e4m3 and

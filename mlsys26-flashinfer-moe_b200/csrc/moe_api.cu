@@ -113,6 +113,7 @@ Layout make_layout(const MoeFwdArgs* a) {
   w.out_f32 = take(sizeof(float) * T * H);
   w.assign_row = take(sizeof(int) * T * K);
   w.rows_out = take(deterministic(a) ? sizeof(float) * static_cast<size_t>(npad) * H : 0);
+  w.inter_bf16 = take(a->gemm2_weights_bf16 ? 2 * static_cast<size_t>(npad) * I : 0);
   w.total_bytes = off;
   return L;
 }
@@ -231,7 +232,8 @@ int check_args(const MoeFwdArgs* a, Layout* L) {
   if (!a->workspace || a->workspace_bytes < L->w.total_bytes) return MOE_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return MOE_ERR_ALIGNMENT;
   if (!aligned16(a->hidden_states) || !aligned16(a->gemm1_weights) ||
-      !aligned16(a->gemm2_weights) || !aligned16(a->output) || !aligned16(a->routing_logits))
+      !aligned16(a->gemm2_weights) || !aligned16(a->output) || !aligned16(a->routing_logits) ||
+      !aligned16(a->gemm2_weights_bf16))
     return MOE_ERR_ALIGNMENT;
   return MOE_OK;
 }
@@ -347,13 +349,21 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   }
 
   const bool small = use_small_path(a);
+  // Prepared bf16 W2 (prefill path only; decode streams the FP8 weights).
+  const bool bf16_w2 = a->gemm2_weights_bf16 != nullptr && !small;
 
   const uint32_t tok_box = small ? 16u : static_cast<uint32_t>(kTileM);
   CUtensorMap tm_a1, tm_b1, tm_a2, tm_b2;
   if ((st = byte_tile_map(pp.a_perm, H, w.npad, &tm_a1, tok_box))) return st;
   if ((st = byte_tile_map(a->gemm1_weights, H, El * 2 * I, &tm_b1))) return st;
-  if ((st = byte_tile_map(ws_ptr<uint8_t>(a, w.inter), I, w.npad, &tm_a2, tok_box))) return st;
-  if ((st = byte_tile_map(a->gemm2_weights, I, El * H, &tm_b2))) return st;
+  if (bf16_w2) {
+    // bf16 matrices read as byte matrices: 128-byte boxes hold 64 elements of K.
+    if ((st = byte_tile_map(ws_ptr<uint8_t>(a, w.inter_bf16), 2 * I, w.npad, &tm_a2))) return st;
+    if ((st = byte_tile_map(a->gemm2_weights_bf16, 2 * I, El * H, &tm_b2))) return st;
+  } else {
+    if ((st = byte_tile_map(ws_ptr<uint8_t>(a, w.inter), I, w.npad, &tm_a2, tok_box))) return st;
+    if ((st = byte_tile_map(a->gemm2_weights, I, El * H, &tm_b2))) return st;
+  }
 
   GemmParams g1{};
   g1.tile_start = pp.tile_start;
@@ -371,6 +381,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   g1.inter_scale = ws_ptr<float>(a, w.inter_scale);
   g1.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
   g1.wait_limit_us = wait_limit_us(a->wait_limit_ns);
+  g1.inter_bf16 = bf16_w2 ? ws_ptr<__nv_bfloat16>(a, w.inter_bf16) : nullptr;
   g1.stall = (a->flags & MOE_FLAG_TEST_STALL) != 0 ? 1 : 0;
   if (small) {
     if ((st = launch_gemm_small(kGemm1, tm_b1, tm_a1, g1, dev->sms, s))) return st;
@@ -391,7 +402,9 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   g2.row_weight = pp.row_weight;
   g2.out_f32 = out_f32;
   g2.stall = 0;
+  g2.inter_bf16 = nullptr;
   g2.rows_out = det ? ws_ptr<float>(a, w.rows_out) : nullptr;
+  if (bf16_w2) g2.num_k_blocks = static_cast<int>(2 * I / kBlockK);   // 64 bf16 per block
   const bool fuse_final = small && !T_dev && !det && T <= kFuseFinalMaxTokens;
   if (fuse_final) {
     g2.final_out = static_cast<__nv_bfloat16*>(a->output);
@@ -400,7 +413,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   if (small) {
     g2.n_tiles = static_cast<int>(H / kTileM);
     if ((st = launch_gemm_small(kGemm2, tm_b2, tm_a2, g2, dev->sms, s))) return st;
-  } else if ((st = launch_gemm(kGemm2, tm_a2, tm_b2, g2, dev->sms, s))) {
+  } else if ((st = launch_gemm(bf16_w2 ? kGemm2Bf16 : kGemm2, tm_a2, tm_b2, g2, dev->sms, s))) {
     return st;
   }
   if ((st = record(ev, 4, s))) return st;
@@ -542,6 +555,19 @@ const char* moe_fp8_status_string(int code) {
     case MOE_ERR_TOO_LARGE: return "size exceeds the fixed scratch of moe_fp8_route_noalloc";
     default: return "unknown status";
   }
+}
+
+int moe_fp8_prepare_gemm2_bf16(const void* w2, const float* w2_scale, int64_t E_local, int64_t H,
+                               int64_t I, void* out, void* stream) {
+  if (E_local < 1 || H < 128 || H % 128 != 0 || I < 128 || I % 128 != 0) return MOE_ERR_SHAPE;
+  if (!w2 || !w2_scale || !out) return MOE_ERR_INVALID_ARG;
+  if (!aligned16(w2) || !aligned16(out) || (reinterpret_cast<uintptr_t>(w2_scale) & 3u) != 0)
+    return MOE_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  const int st = device_info(&dev);
+  if (st) return st;
+  return launch_prepare_w2_bf16(w2, w2_scale, E_local, H, I, out, dev->sms,
+                                static_cast<cudaStream_t>(stream));
 }
 
 int moe_bf16_to_fp8_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale,

@@ -262,6 +262,34 @@ __host__ __device__ constexpr uint32_t umma_idesc_e4m3_f32(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
 
+// Instruction descriptor: bf16 x bf16 -> fp32 (kind::f16), both operands K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n) {
+  return (1u << 4)                                  // D format f32
+         | (1u << 7) | (1u << 10)                   // A, B = bf16
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+// Four bf16 MMAs of K=16 each (one 128-byte row of the swizzled K-major tiles:
+// the descriptors of the slices are the stage's plus 32 bytes each, i.e. +2 in
+// the start-address field), D (+)= A*B^T; `accumulate` = 0 starts D over with
+// the first of them.
+__device__ __forceinline__ void umma_bf16_x4(uint32_t d_tmem, uint64_t a, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred f, t;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "setp.ne.b32 f, %4, 0;\n\t"
+      "setp.eq.b32 t, %3, %3;\n\t"
+      "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, f;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, t;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, t;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, t;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by a single thread.
 __device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                         uint32_t idesc, uint32_t accumulate) {

@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kMode == kGemm1 ? 1 : 2);   // one commit per scale group
+      mbar_init(&empty[s], kMode == kGemm2 ? 2 : 1);   // one commit per scale group
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -198,7 +198,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // "released" barrier and visits the stages in K order, so no barrier it
     // waits on is ever more than one phase ahead (the parity waits need that),
     // and the cost of issuing is split over two sub-partitions.
-    if (lane == 0) {
+    if constexpr (kMode == kGemm2Bf16) {
+      // bf16 operands carry no block scales: warp 9 accumulates a unit's whole K
+      // range into one TMEM buffer (unit parity), four K=16 MMAs per 128-byte
+      // stage, and commits the buffer once per unit; warp 10 only joins the
+      // drain.
+      if (lane == 0 && warp == 9) {
+        const uint32_t idesc = umma_idesc_bf16_f32(kTileM, kTileN);
+        const uint64_t a_desc0 = umma_desc_sw128(smem_u32(sA));
+        const uint64_t b_desc0 = umma_desc_sw128(smem_u32(sB));
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t ui = 0;
+        for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++ui) {
+          const uint32_t buf = ui & 1u;
+          if (!mbar_wait(&tempty[buf], ((ui >> 1) & 1u) ^ 1u, abort_flag, p.ctrl, 7))
+            goto mma_done;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + buf * kTileN;
+#pragma unroll 1
+          for (int kb = 0; kb < KB; ++kb) {
+            const uint64_t a_d = a_desc0 + ((static_cast<uint32_t>(stage) * kStageABytes) >> 4);
+            const uint64_t b_d = b_desc0 + ((static_cast<uint32_t>(stage) * kStageBBytes) >> 4);
+            if (!mbar_wait(&full[stage], phase, abort_flag, p.ctrl, 8)) goto mma_done;
+            tc_fence_after();
+            umma_bf16_x4(d_tmem, a_d, b_d, idesc, kb > 0 ? 1u : 0u);
+            umma_commit(&empty[stage]);
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          umma_commit(&tfull[buf]);
+        }
+      }
+    } else if (lane == 0) {
       constexpr int kGroups = kMode == kGemm1 ? 1 : 2;   // scale blocks per K block
       constexpr int kMmaPerGroup = (kBlockK / 32) / kGroups;
       const uint32_t me = static_cast<uint32_t>(warp - 9);   // = the buffer it fills
@@ -246,6 +280,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+    }
+    if (lane == 0) {
     mma_done:
       // Commits of one issuer arrive in order; once both issuers' drain
       // commits have landed, every MMA and barrier arrival is done and TMEM /
@@ -333,10 +369,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           const float sc = fmaxf(amax / 448.0f, 1e-12f);
           const float inv = 1.0f / sc;
+          uint8_t* stg = xpose + warp * kXposeBytesPerWarp;
+          if (p.inter_bf16 != nullptr) {
+            // For the bf16 GEMM2: the same FP8 codes, dequantised (code * scale)
+            // and rounded to bf16; 128 bytes per row, through the staging tile
+            // in two passes of 32 values.
+#pragma unroll
+            for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll
+              for (int q16 = 0; q16 < 4; ++q16) {
+                uint32_t w4[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float* a2 = acc + 32 * pass + 8 * q16 + 2 * j;
+                  const __nv_fp8x2_storage_t codes =
+                      static_cast<__nv_fp8x2_storage_t>(pack_e4m3x2(a2[0] * inv, a2[1] * inv));
+                  const float2 f =
+                      __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(codes, __NV_E4M3)));
+                  const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+                  w4[j] = *reinterpret_cast<const uint32_t*>(&b);
+                }
+                *reinterpret_cast<uint4*>(stg + xpose_off(lane, q16)) =
+                    make_uint4(w4[0], w4[1], w4[2], w4[3]);
+              }
+              __syncwarp();
+              uint8_t* dstb = reinterpret_cast<uint8_t*>(p.inter_bf16) +
+                              2 * (static_cast<int64_t>(c.row0 + q * 32) * p.inter +
+                                   c.n * (kTileN / 2) + 64 * h + 32 * pass) +
+                              16 * (lane & 3);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int rr = 8 * i + (lane >> 2);
+                if (q * 32 + rr < c.nrows)
+                  *reinterpret_cast<uint4*>(dstb + 2 * static_cast<int64_t>(rr) * p.inter) =
+                      *reinterpret_cast<const uint4*>(stg + xpose_off(rr, lane & 3));
+              }
+              __syncwarp();
+            }
+          } else {
           // Each lane's 64 FP8 codes go through the warp's staging tile; the
           // stores then write 64 contiguous bytes of 8 rows per instruction
           // instead of 16 bytes of 32 rows.
-          uint8_t* stg = xpose + warp * kXposeBytesPerWarp;
 #pragma unroll
           for (int q16 = 0; q16 < 4; ++q16) {
             uint32_t w4[4];
@@ -360,8 +433,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           __syncwarp();
           if (row_valid) p.inter_scale[static_cast<int64_t>(2 * c.n + h) * p.npad + grow] = sc;
+          }
         }
       } else {
+        if constexpr (kMode == kGemm2Bf16) {
+          // The unit's whole K range was accumulated in TMEM buffer (unit
+          // parity): one wait, 128 columns read, the buffer released.
+          const uint32_t buf = g & 1u;
+          if (!mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 6)) goto epi_done;
+          tc_fence_after();
+          if (warp_active) {
+            const uint32_t tb = t_lane + buf * kTileN + 128u * h;
+            tmem_ld32(tb, acc);
+            tmem_ld32(tb + 32, acc + 32);
+            tmem_ld_wait();
+            tmem_ld32(tb + 64, acc + 64);
+            tmem_ld32(tb + 96, acc + 96);
+            tmem_ld_wait();
+          }
+          release_buffer(&tempty[buf], lane);
+          ++g;
+        } else {
         // W2 scale [E, H/128, I/128]: row block 2n + h of this thread's columns.
         const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * kb_rows + 2 * c.n + h) * KB;
         // Both intermediate scales of K block kb+1 and its weight scale are
@@ -408,6 +500,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             ++g;
           }
+        }
         }
         // Routing-weighted scatter-add into out[token] (kernel.py:236-250).
         // Every row goes to a different token, so a lane-per-row red.v4
@@ -478,6 +571,9 @@ int gemm_set_smem_attrs() {
   if (cudaFuncSetAttribute(moe_gemm_kernel<kGemm2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            smem) != cudaSuccess)
     return MOE_ERR_CUDA;
+  if (cudaFuncSetAttribute(moe_gemm_kernel<kGemm2Bf16>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return MOE_ERR_CUDA;
   return MOE_OK;
 }
 
@@ -486,8 +582,10 @@ int launch_gemm(int mode, const CUtensorMap& tm_a, const CUtensorMap& tm_b, cons
   const int smem = gemm_smem_bytes();
   if (mode == kGemm1)
     moe_gemm_kernel<kGemm1><<<grid, kGemmThreads, smem, stream>>>(tm_a, tm_b, p);
-  else
+  else if (mode == kGemm2)
     moe_gemm_kernel<kGemm2><<<grid, kGemmThreads, smem, stream>>>(tm_a, tm_b, p);
+  else
+    moe_gemm_kernel<kGemm2Bf16><<<grid, kGemmThreads, smem, stream>>>(tm_a, tm_b, p);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 

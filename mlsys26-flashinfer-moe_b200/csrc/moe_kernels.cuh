@@ -94,6 +94,8 @@ struct GemmParams {
   int64_t final_n8;        // T * H / 8
   float* rows_out;         // GEMM2, deterministic combine: [npad, H] weighted rows, stored
                            // instead of added into out_f32
+  __nv_bfloat16* inter_bf16;  // GEMM1 with prepared bf16 W2: [npad, I] dequantised
+                              // intermediate (bf16(code * scale)) instead of codes + scales
   unsigned int wait_limit_us;         // bound of the bounded waits (wait_limit_us())
   int stall;               // GEMM1, failure-detection tests: first MMA issuer waits forever
   CtrlBlock* ctrl;
@@ -113,6 +115,10 @@ __global__ void moe_combine_rows_kernel(const float* __restrict__ rows_out,
 
 constexpr int kGemm1 = 0;   // gate/up GEMM, SwiGLU + 1x64 FP8 requant epilogue
 constexpr int kGemm2 = 1;   // down GEMM, routing-weighted scatter-add epilogue
+// down GEMM on bf16 operands (the dequantised intermediate and a prepared
+// bf16(W2 * block scale)): no block scales left, so the tensor core accumulates
+// all of K in TMEM and there is no promotion; same epilogue as kGemm2.
+constexpr int kGemm2Bf16 = 2;
 
 // Host-side launchers defined next to the kernel templates (moe_gemm.cu).
 int gemm_set_smem_attrs();
@@ -143,6 +149,10 @@ int route_only(const MoeFwdArgs* a, cudaStream_t s);
 // SM count of the current device (checks that it is an sm_100 part).
 int num_sms(int* out);
 MoeWorkspaceLayout workspace_layout_for(const MoeFwdArgs* a);
+
+// bf16(W2 * block scale) for the bf16 GEMM2 (moe_quant.cu).
+int launch_prepare_w2_bf16(const void* w2, const float* w2s, int64_t E, int64_t H, int64_t I,
+                           void* out, int sms, cudaStream_t stream);
 
 // bf16 -> e4m3 1x128 activation quantisation (moe_quant.cu).
 int launch_quant_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale, int sms,

@@ -61,4 +61,62 @@ int launch_quant_1x128(const void* x, int64_t T, int64_t H, void* q, float* scal
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
+// ---------------------------------------------------------------------------
+// One-time relayout of the down-projection weights for the bf16 GEMM2:
+// out[e, h, i] = bf16(float(W2[e, h, i]) * W2_scale[e, h/128, i/128]), i.e. the
+// reference's dequantised weight (kernel.py:224-234 multiplies the FP8 dot by
+// this block scale) rounded once to bf16.  Each thread converts 16 codes (one
+// 16-byte load, two 16-byte stores); the 16 share one scale block because
+// 16 divides 128.  Memory-bound: 3 bytes per element.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+__global__ void __launch_bounds__(256)
+    moe_prepare_w2_bf16_kernel(const uint8_t* __restrict__ w, const float* __restrict__ s,
+                               __nv_bfloat16* __restrict__ out, int64_t n16, int64_t H,
+                               int64_t I) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t hi_blocks = H / 128, ii_blocks = I / 128;
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < n16;
+       c += stride) {
+    const int64_t off = c * 16;
+    const int64_t e = off / (H * I);
+    const int64_t rem = off - e * H * I;
+    const int64_t h = rem / I;
+    const int64_t i = rem - h * I;
+    const float sc = __ldg(s + (e * hi_blocks + h / 128) * ii_blocks + i / 128);
+    const uint4 codes = __ldcs(reinterpret_cast<const uint4*>(w) + c);
+    const uint32_t wd[4] = {codes.x, codes.y, codes.z, codes.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const __nv_fp8x2_storage_t two =
+            static_cast<__nv_fp8x2_storage_t>((wd[k] >> (16 * half)) & 0xffffu);
+        const float2 f = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(two, __NV_E4M3)));
+        const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+        o[2 * k + half] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + off);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+}  // namespace
+
+int launch_prepare_w2_bf16(const void* w2, const float* w2s, int64_t E, int64_t H, int64_t I,
+                           void* out, int sms, cudaStream_t stream) {
+  const int64_t n16 = E * H * I / 16;
+  int64_t blocks = (n16 + 255) / 256;
+  if (blocks > static_cast<int64_t>(sms) * 8) blocks = static_cast<int64_t>(sms) * 8;
+  if (blocks < 1) blocks = 1;
+  moe_prepare_w2_bf16_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
+      static_cast<const uint8_t*>(w2), w2s, static_cast<__nv_bfloat16*>(out), n16, H, I);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
 }  // namespace moe

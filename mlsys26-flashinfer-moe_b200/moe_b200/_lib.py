@@ -60,6 +60,7 @@ class MoeFwdArgs(ctypes.Structure):
         ("flags", ctypes.c_uint32),
         ("reserved", ctypes.c_uint32),
         ("wait_limit_ns", ctypes.c_uint64),
+        ("gemm2_weights_bf16", ctypes.c_void_p),
     ]
 
 
@@ -84,6 +85,7 @@ class MoeWorkspaceLayout(ctypes.Structure):
         ("out_f32", ctypes.c_size_t),
         ("assign_row", ctypes.c_size_t),
         ("rows_out", ctypes.c_size_t),
+        ("inter_bf16", ctypes.c_size_t),
     ]
 
 
@@ -115,6 +117,9 @@ SYMBOLS = {
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "moe_bf16_to_fp8_1x128": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "moe_fp8_prepare_gemm2_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                                  ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+                                                  ctypes.c_void_p]),
     "moe_ep_create": (ctypes.c_int, [ctypes.POINTER(MoeEpConfig), ctypes.POINTER(_VP)]),
     "moe_ep_ipc_handle": (ctypes.c_int, [_VP, _VP]),
     "moe_ep_connect": (ctypes.c_int, [_VP, ctypes.c_char_p]),

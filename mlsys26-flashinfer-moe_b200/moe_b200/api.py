@@ -60,12 +60,14 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                local_expert_offset: int, routed_scaling_factor: float, output: torch.Tensor,
                n_group: int = 8, topk_group: int = 4, top_k: int = 8,
-               deterministic: bool = False):
+               deterministic: bool = False, gemm2_weights_bf16: Optional[torch.Tensor] = None):
     """Validate like the reference and fill a ``MoeFwdArgs`` (no workspace yet).
 
     ``deterministic`` selects the fixed-order combine (``MOE_FLAG_DETERMINISTIC``):
     bit-identical output from run to run, at the cost of one fp32 row per
-    (token, expert) assignment in the workspace.
+    (token, expert) assignment in the workspace.  ``gemm2_weights_bf16``: the
+    same down-projection weights prepared by ``prepare_gemm2_weights`` (bf16
+    GEMM2 without block-scale promotion on the prefill path).
 
     Returns ``(args, keepalive, out_dev)``: ``keepalive`` holds the device
     copies the pointers refer to; ``out_dev`` is where the kernel writes (the
@@ -119,6 +121,13 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     a.routed_scaling_factor = float(routed_scaling_factor)
     a.bias_dtype = _BIAS_DTYPES[routing_bias.dtype]
     a.flags = _lib.MOE_FLAG_DETERMINISTIC if deterministic else 0
+    if gemm2_weights_bf16 is not None:
+        assert gemm2_weights_bf16.dtype == torch.bfloat16 and \
+            gemm2_weights_bf16.shape == (e_local, h, i), \
+            f"gemm2_weights_bf16 must be bf16 [{e_local}, {h}, {i}] (prepare_gemm2_weights)"
+        wb = _to_device(gemm2_weights_bf16, device)
+        tensors.append(wb)
+        a.gemm2_weights_bf16 = wb.data_ptr()
     return a, tensors, out_dev
 
 
@@ -167,7 +176,8 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
         gemm2_weights_scale: torch.Tensor, local_expert_offset: int,
         routed_scaling_factor: float, output: torch.Tensor, *, n_group: int = 8,
         topk_group: int = 4, top_k: int = 8, workspace: Optional[torch.Tensor] = None,
-        deterministic: bool = False) -> None:
+        deterministic: bool = False,
+        gemm2_weights_bf16: Optional[torch.Tensor] = None) -> None:
     """Fused FP8 block-scale DeepSeek-V3 MoE forward (reference ``kernel.py:562``).
 
     Writes the bf16 ``[T, H]`` layer output into ``output``.  Only the experts
@@ -176,18 +186,44 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     avoid the internal per-stream cache.  ``deterministic=True`` adds each
     token's expert rows in a fixed order (bit-identical runs) instead of with
     fp32 atomics as the reference does (kernel.py:246-250).
+    ``gemm2_weights_bf16`` (from ``prepare_gemm2_weights(gemm2_weights,
+    gemm2_weights_scale)``, made once for a layer's weights) runs the prefill
+    GEMM2 on bf16 operands; decode-sized batches ignore it.
     """
     args, keep, out_dev = build_args(routing_logits, routing_bias, hidden_states,
                                      hidden_states_scale, gemm1_weights, gemm1_weights_scale,
                                      gemm2_weights, gemm2_weights_scale, local_expert_offset,
                                      routed_scaling_factor, output, n_group, topk_group, top_k,
-                                     deterministic)
+                                     deterministic, gemm2_weights_bf16)
     device = keep[0].device
     if args.T > 0:
         forward_args(args, workspace, device)
     if out_dev is not output:
         output.copy_(out_dev)
     return None
+
+
+def prepare_gemm2_weights(gemm2_weights: torch.Tensor, gemm2_weights_scale: torch.Tensor,
+                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One-time relayout of a layer's down-projection weights for the bf16
+    GEMM2: ``bf16(W2 * block scale)`` as ``[E_local, H, I]`` (twice the bytes of
+    the FP8 weights).  Pass the result to ``run(..., gemm2_weights_bf16=...)``
+    for every forward with these weights."""
+    assert gemm2_weights.dtype == _F8 and gemm2_weights.dim() == 3, "gemm2_weights must be e4m3 [E, H, I]"
+    assert gemm2_weights.is_cuda, "gemm2_weights must be a CUDA tensor"
+    e, h, i = (int(x) for x in gemm2_weights.shape)
+    assert gemm2_weights_scale.dtype == torch.float32 and \
+        gemm2_weights_scale.shape == (e, h // 128, i // 128)
+    w = gemm2_weights.contiguous()
+    s = gemm2_weights_scale.to(w.device).contiguous()
+    if out is None:
+        out = torch.empty(e, h, i, dtype=torch.bfloat16, device=w.device)
+    stream = torch.cuda.current_stream(w.device)
+    code = _lib.load().moe_fp8_prepare_gemm2_bf16(w.data_ptr(), s.data_ptr(), e, h, i,
+                                                 out.data_ptr(), ctypes.c_void_p(stream.cuda_stream))
+    if code:
+        _raise(code, "moe_fp8_prepare_gemm2_bf16")
+    return out
 
 
 def quantize_1x128(x: torch.Tensor, q: Optional[torch.Tensor] = None,

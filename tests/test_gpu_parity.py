@@ -408,3 +408,83 @@ def test_routing_exact_ties_match_the_oracle(cuda_device):
             inp["routing_bias"] = torch.from_numpy(b).cuda()
             _, views, _ = run_cuda(inp, shape)
             check_routing_and_dispatch(views, inp, shape)
+
+
+# ---------------------------------------------------------------- prepared bf16 W2
+
+def test_prepare_gemm2_weights_is_bf16_of_the_dequantised_weight(cuda_device):
+    from moe_b200 import prepare_gemm2_weights
+    shape = workloads.MoeShape(t=1, hidden=1024, inter=384, e_global=64, e_local=8, n_group=8,
+                               topk_group=2, top_k=6)
+    inp = workloads.make_inputs(shape, seed=801, device="cuda")
+    w, s = inp["gemm2_weights"], inp["gemm2_weights_scale"]
+    got = prepare_gemm2_weights(w, s)
+    e, h, i = w.shape
+    ref = (w.float().view(e, h // 128, 128, i // 128, 128) *
+           s.view(e, h // 128, 1, i // 128, 1)).view(e, h, i).to(torch.bfloat16)
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("case", ["dsv3_2048", "odd_700", "contest_901"])
+def test_prepared_bf16_gemm2_prefill(cuda_device, case):
+    """GEMM2 on bf16 operands (prepared W2, dequantised intermediate): routing
+    unchanged; output against the oracle and, at DeepSeek-V3 size, every element
+    against the fp32 PyTorch layer.  bf16 rounds each GEMM2 operand once more
+    (2^-9 relative), so the bar is the north star's cosine >= 0.9999 with at
+    most 0.1% of the elements outside allclose(1e-2, 2e-2) (observed: 0.014% of
+    a sample, the largest 0.015 off) and none further off than 0.05."""
+    from moe_b200 import prepare_gemm2_weights, run
+    if case == "dsv3_2048":
+        inp, shape = dsv3_inputs(2048, seed=17)
+    elif case == "contest_901":
+        inp, shape = dsv3_inputs(901, seed=32, e_local=32, local_expert_offset=32)
+    else:
+        shape = workloads.MoeShape(t=700, hidden=1024, inter=384, e_global=64, e_local=64,
+                                   n_group=8, topk_group=2, top_k=6)
+        inp = workloads.make_inputs(shape, seed=1000, device="cuda")
+    wb = prepare_gemm2_weights(inp["gemm2_weights"], inp["gemm2_weights_scale"])
+    out = torch.empty(shape.t, shape.hidden, dtype=torch.bfloat16, device="cuda")
+    run(*workloads.run_args(inp), out, n_group=shape.n_group, topk_group=shape.topk_group,
+        top_k=shape.top_k, gemm2_weights_bf16=wb)
+    out_fp8, views, _ = run_cuda(inp, shape)
+    torch.cuda.synchronize()
+    check_routing_and_dispatch(views, inp, shape)
+    toks = np.random.default_rng(shape.t).choice(shape.t, 6, replace=False)
+    ref = oracle_output(inp, shape, tokens=toks)
+    got = bf16_np(out)[toks]
+    assert mo.cosine(got, ref) >= COS
+    d = np.abs(got.astype(np.float64) - ref)
+    assert np.mean(d > ATOL + RTOL * np.abs(ref)) <= 1e-3 and d.max() <= 0.05
+    g, f = out.float(), out_fp8.float()
+    assert (torch.dot(g.flatten(), f.flatten()) / (g.norm() * f.norm())).item() >= 0.99999
+    if case == "dsv3_2048":
+        ref_t = torch_fp32_layer(inp, shape, views["topk_idx"], views["topk_weights"])
+        diff = (g - ref_t).abs()
+        outside = diff > ATOL + RTOL * ref_t.abs()
+        assert outside.float().mean().item() <= 1e-3, int(outside.sum())
+        assert diff.max().item() <= 0.05
+        cos = torch.dot(g.flatten(), ref_t.flatten()) / (g.norm() * ref_t.norm())
+        assert cos.item() >= COS
+
+
+def test_prepared_bf16_gemm2_deterministic_and_decode(cuda_device):
+    """The bf16 GEMM2 with the deterministic combine gives the same bits twice;
+    a decode-sized batch ignores the prepared weights (FP8 decode GEMMs)."""
+    from moe_b200 import prepare_gemm2_weights, run
+    inp, shape = dsv3_inputs(600, seed=33, e_local=64, local_expert_offset=0)
+    wb = prepare_gemm2_weights(inp["gemm2_weights"], inp["gemm2_weights_scale"])
+    outs = []
+    for _ in range(2):
+        o = torch.empty(shape.t, shape.hidden, dtype=torch.bfloat16, device="cuda")
+        run(*workloads.run_args(inp), o, deterministic=True, gemm2_weights_bf16=wb)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    inp8, shape8 = dsv3_inputs(8, seed=34, e_local=64, local_expert_offset=0)
+    wb8 = prepare_gemm2_weights(inp8["gemm2_weights"], inp8["gemm2_weights_scale"])
+    a = torch.empty(8, shape8.hidden, dtype=torch.bfloat16, device="cuda")
+    b = torch.empty_like(a)
+    run(*workloads.run_args(inp8), a, deterministic=True, gemm2_weights_bf16=wb8)
+    run(*workloads.run_args(inp8), b, deterministic=True)
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
