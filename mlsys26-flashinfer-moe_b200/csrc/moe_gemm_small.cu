@@ -217,11 +217,15 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_tok);
   }
-  // Everything above only touches this CTA's own resources; the routing
-  // tables and every later read come from the kernels before this one, which
-  // (under programmatic dependent launch) may still be finishing.
-  griddep_launch_dependents();
-  griddep_wait();
+  // Everything above only touches this CTA's own resources.  GEMM1 waits for
+  // the routing kernels (programmatic dependent launch) before it lets GEMM2
+  // launch, so when GEMM2 starts the routing tables are complete: GEMM2 reads
+  // them, and streams its first weight tiles, before it waits for GEMM1 (see
+  // the producer); everything GEMM1 writes is read after that wait.
+  if constexpr (kMode == kGemm1) {
+    griddep_wait();
+    griddep_launch_dependents();
+  }
   for (int i = threadIdx.x; i < E; i += kSmallThreads) {
     counts_s[i] = p.counts[i];
     tstart_s[i] = p.tile_start[i];
@@ -261,6 +265,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   // Split units add partial products, which the deterministic combine's
   // stored rows cannot take.
   const SegSpace segs = make_seg_space(total_units, KB, kMode == kGemm2 && p.rows_out == nullptr);
+  if constexpr (kMode == kGemm2) {
+    griddep_launch_dependents();
+    if (!(warp == 4 && lane == 0)) griddep_wait();   // the producer waits after its early loads
+  }
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
@@ -268,17 +276,37 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0, issued_phase = 0;
+      // GEMM2: the weight boxes of the first S stages (items 0..S-1 of this
+      // CTA, stages 0..S-1 of the first ring pass) go out before the wait for
+      // GEMM1; the items' token boxes, which GEMM1 writes, after it.  Each
+      // stage's barrier expects both boxes either way.
+      int early = 0;
+      if constexpr (kMode == kGemm2) {
+        for (Seg sg = segs.first(); sg.u >= 0 && early < S; sg = segs.next(sg)) {
+          const SmallUnit c = decode_small(sg.u, ustart_s, counts_s, tstart_s, E, NT);
+          const int w_row0 = c.e * p.b_rows_per_expert + c.n * kTileM;
+          for (int kb = sg.kb0; kb < sg.kb1 && early < S; ++kb, ++early) {
+            mbar_arrive_expect_tx(&full[early], Cfg::kStageBytes);
+            tma_load_2d(sW + early * Cfg::kWBytes, &tm_w, &full[early], kb * kBlockK, w_row0);
+            issued |= 1u << early;
+          }
+        }
+        griddep_wait();
+      }
+      int item = 0;
       for (Seg sg = segs.first(); sg.u >= 0; sg = segs.next(sg)) {
         const SmallUnit c = decode_small(sg.u, ustart_s, counts_s, tstart_s, E, NT);
         const int w_row0 = c.e * p.b_rows_per_expert + c.n * kTileM;
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 11)) goto producer_done;
-          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          uint8_t* w_dst = sW + stage * Cfg::kWBytes;
-          tma_load_2d(w_dst, &tm_w, &full[stage], kb * kBlockK, w_row0);
-          if constexpr (kMode == kGemm1)
-            tma_load_2d(w_dst + kTileM * kBlockK, &tm_w, &full[stage], kb * kBlockK,
-                        w_row0 + p.inter);
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++item) {
+          if (item >= early) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.ctrl, 11)) goto producer_done;
+            mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+            uint8_t* w_dst = sW + stage * Cfg::kWBytes;
+            tma_load_2d(w_dst, &tm_w, &full[stage], kb * kBlockK, w_row0);
+            if constexpr (kMode == kGemm1)
+              tma_load_2d(w_dst + kTileM * kBlockK, &tm_w, &full[stage], kb * kBlockK,
+                          w_row0 + p.inter);
+          }
           tma_load_2d(sT + stage * kTokBytes, &tm_tok, &full[stage], kb * kBlockK, c.row0);
           issued |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
