@@ -49,6 +49,8 @@ extern "C" {
 #define MOE_ERR_TIMEOUT (-6)         /* a device-side bounded wait expired */
 #define MOE_ERR_DEVICE (-7)          /* device is not sm_100 */
 #define MOE_ERR_TOO_LARGE (-8)       /* beyond the fixed scratch of moe_fp8_route_noalloc */
+#define MOE_ERR_BOUNDS (-9)          /* MOE_FLAG_DEBUG: a dispatch table or a workspace guard
+                                        failed its check; info = MOE_CHECK_* << 24 | index */
 
 /* routing_bias element type */
 #define MOE_BIAS_F32 0
@@ -63,6 +65,15 @@ extern "C" {
  * (kernel.py:246-250).  Costs one extra fp32 write and read per assignment row
  * (rows_out in the workspace). */
 #define MOE_FLAG_DETERMINISTIC 0x1u
+/* Debug bounds checks.  The forward writes a 16-byte guard pattern after every
+ * workspace buffer, checks the routing and dispatch tables on the device before
+ * any kernel uses them as indices (moe_fp8_check_workspace's checks), lets the
+ * GEMMs do no work when a check failed, and checks the guards after the last
+ * kernel.  A failure records MOE_ERR_BOUNDS with info = (MOE_CHECK_* << 24) |
+ * the failing element's index (clamped to 24 bits) in the control block; read it
+ * with moe_fp8_device_error.  The output is not meaningful after a failure.  The
+ * reference has no counterpart (its kernels index without checks). */
+#define MOE_FLAG_DEBUG 0x2u
 /* Failure-detection tests only: the first MMA issuer of each GEMM1 CTA waits
  * on a barrier that nothing completes, so its bounded wait runs out after
  * wait_limit_ns; the layer then drains, records MOE_ERR_TIMEOUT (info = the
@@ -163,6 +174,27 @@ int moe_fp8_route(const MoeFwdArgs* a, void* stream);
 /* Device-side error word of the last forward on this workspace (0 = none).
  * Reads the control block with a blocking copy on `stream`. */
 int moe_fp8_device_error(const MoeFwdArgs* a, void* stream, int32_t* code, int32_t* info);
+
+/* What failed, in bits 24-31 of the info word of MOE_ERR_BOUNDS; bits 0-23
+ * hold the index of the failing element (expert, assignment t*top_k+k, row or
+ * guard number). */
+#define MOE_CHECK_COUNTS 1       /* counts[e] outside [0, T] */
+#define MOE_CHECK_TILE_START 2   /* tile_start not the 128-row prefix of counts, or past npad */
+#define MOE_CHECK_TOPK_IDX 3     /* routed expert id outside [0, E_global) or repeated in a token */
+#define MOE_CHECK_TOPK_WEIGHT 4  /* routing weight not finite */
+#define MOE_CHECK_ROW_TOKEN 5    /* a live permuted row's token outside [0, T) */
+#define MOE_CHECK_ROW_WEIGHT 6   /* a live row's weight differs from its assignment's */
+#define MOE_CHECK_ROW_EXPERT 7   /* a live row's token was not routed to the row's expert */
+#define MOE_CHECK_ASSIGN_ROW 8   /* an assignment's row is not the live row holding it */
+#define MOE_CHECK_GUARD 9        /* the guard after workspace buffer `index` was overwritten */
+
+/* Checks the routing and dispatch tables that the last forward left in the
+ * workspace, and, when a->flags has MOE_FLAG_DEBUG (the last forward wrote the
+ * guards), the workspace guards.  Clears the control block's error word first;
+ * the result is read with moe_fp8_device_error.  Reads the tables only with
+ * indices it has checked, so it is safe on any workspace contents.  Asynchronous
+ * on `stream`.  No counterpart in the reference (debugging aid). */
+int moe_fp8_check_workspace(const MoeFwdArgs* a, void* stream);
 
 /* Routing for callers that cannot allocate device memory.  No counterpart in
  * the reference.

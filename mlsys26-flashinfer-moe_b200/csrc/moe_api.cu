@@ -45,18 +45,21 @@ int validate_shape(const MoeFwdArgs* a) {
   if (a->bias_dtype != MOE_BIAS_F32 && a->bias_dtype != MOE_BIAS_BF16 &&
       a->bias_dtype != MOE_BIAS_F16)
     return MOE_ERR_INVALID_ARG;
-  if ((a->flags & ~(MOE_FLAG_DETERMINISTIC | MOE_FLAG_TEST_STALL)) != 0 || a->reserved != 0)
+  if ((a->flags & ~(MOE_FLAG_DETERMINISTIC | MOE_FLAG_DEBUG | MOE_FLAG_TEST_STALL)) != 0 ||
+      a->reserved != 0)
     return MOE_ERR_INVALID_ARG;
   return MOE_OK;
 }
 
 bool deterministic(const MoeFwdArgs* a) { return (a->flags & MOE_FLAG_DETERMINISTIC) != 0; }
+bool debug_checks(const MoeFwdArgs* a) { return (a->flags & MOE_FLAG_DEBUG) != 0; }
 
 struct Layout {
   MoeWorkspaceLayout w;
   int tokens_per_block;
   int blocks;
   int permute_split;   // permute blocks per routing block (grid.y)
+  GuardList guards;    // offsets of the buffers' guards (base set at launch)
 };
 
 // Decode-shaped batches (few rows per expert on average) take the
@@ -92,10 +95,15 @@ Layout make_layout(const MoeFwdArgs* a) {
   w.npad = npad;
   w.route_blocks = L.blocks;
   w.tokens_per_block = tpb;
+  // Every buffer is followed by a 16-byte guard (written and checked only by
+  // MOE_FLAG_DEBUG forwards) before the next 1024-byte boundary.
   size_t off = 0;
+  L.guards.n = 0;
   auto take = [&](size_t bytes) {
     const size_t at = off;
-    off = align_up(off + bytes, kAlign);
+    const size_t guard = align_up(at + bytes, kGuardBytes);
+    L.guards.off[L.guards.n++] = guard;
+    off = align_up(guard + kGuardBytes, kAlign);
     return at;
   };
   w.ctrl = take(sizeof(CtrlBlock));
@@ -279,6 +287,42 @@ int launch_route(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
+CheckParams check_params(const MoeFwdArgs* a, const Layout& L) {
+  const MoeWorkspaceLayout& w = L.w;
+  CheckParams c{};
+  c.T = static_cast<int>(a->T);
+  c.top_k = static_cast<int>(a->top_k);
+  c.E_global = static_cast<int>(a->E_global);
+  c.E_local = static_cast<int>(a->E_local);
+  c.local_expert_offset = static_cast<int>(a->local_expert_offset);
+  c.npad = w.npad;
+  c.counts = ws_ptr<int>(a, w.counts);
+  c.tile_start = ws_ptr<int>(a, w.tile_start);
+  c.topk_idx = ws_ptr<int>(a, w.topk_idx);
+  c.topk_weights = ws_ptr<float>(a, w.topk_weights);
+  c.row_token = ws_ptr<int>(a, w.row_token);
+  c.row_weight = ws_ptr<float>(a, w.row_weight);
+  c.assign_row = ws_ptr<int>(a, w.assign_row);
+  c.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
+  return c;
+}
+
+int launch_check_dispatch(const MoeFwdArgs* a, const Layout& L, int sms, cudaStream_t s) {
+  const CheckParams c = check_params(a, L);
+  const int64_t items = c.E_local + static_cast<int64_t>(c.T) * c.top_k + c.npad;
+  int64_t blocks = (items + 255) / 256;
+  if (blocks > 4 * sms) blocks = 4 * sms;
+  moe_check_dispatch_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(c);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+int launch_guards(const MoeFwdArgs* a, const Layout& L, bool write, cudaStream_t s) {
+  GuardList g = L.guards;
+  g.base = static_cast<uint8_t*>(a->workspace);
+  moe_guard_kernel<<<1, 32, 0, s>>>(g, write ? 1 : 0, ws_ptr<CtrlBlock>(a, L.w.ctrl));
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
 int record(void* const* ev, int i, cudaStream_t s) {
   if (!ev) return MOE_OK;
   return cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
@@ -296,6 +340,10 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   if ((st = record(ev, 0, s))) return st;
   const MoeWorkspaceLayout& w = L.w;
   const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local;
+  // Debug checks (single-GPU forward only; the expert-parallel receive side
+  // passes flags 0).
+  const bool dbg = debug_checks(a) && !T_dev;
+  if (dbg && (st = launch_guards(a, L, true, s))) return st;
   float* out_f32 = ws_ptr<float>(a, w.out_f32);
   PermuteParams pp{};
   pp.T = static_cast<int>(T);
@@ -347,6 +395,9 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
       return MOE_ERR_CUDA;
     if ((st = record(ev, 2, s))) return st;
   }
+  // Tables checked before the GEMMs read them; on a failure the GEMMs see the
+  // error word and schedule no units.
+  if (dbg && (st = launch_check_dispatch(a, L, dev->sms, s))) return st;
 
   const bool small = use_small_path(a);
   // Prepared bf16 W2 (prefill path only; decode streams the FP8 weights).
@@ -383,6 +434,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   g1.wait_limit_us = wait_limit_us(a->wait_limit_ns);
   g1.inter_bf16 = bf16_w2 ? ws_ptr<__nv_bfloat16>(a, w.inter_bf16) : nullptr;
   g1.stall = (a->flags & MOE_FLAG_TEST_STALL) != 0 ? 1 : 0;
+  g1.skip_on_error = dbg ? 1 : 0;
   if (small) {
     if ((st = launch_gemm_small(kGemm1, tm_b1, tm_a1, g1, dev->sms, s))) return st;
   } else if ((st = launch_gemm(kGemm1, tm_a1, tm_b1, g1, dev->sms, s))) {
@@ -418,7 +470,10 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   }
   if ((st = record(ev, 4, s))) return st;
   if (T_dev) return MOE_OK;
-  if (fuse_final) return record(ev, 5, s);
+  if (fuse_final) {
+    if ((st = record(ev, 5, s))) return st;
+    return dbg ? launch_guards(a, L, false, s) : MOE_OK;
+  }
 
   const int64_t n8 = T * H / 8;
   int blocks = static_cast<int>((n8 + 255) / 256);
@@ -435,7 +490,8 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
                             static_cast<const float*>(out_f32),
                             static_cast<__nv_bfloat16*>(a->output), n8);
   if (e != cudaSuccess) return MOE_ERR_CUDA;
-  return record(ev, 5, s);
+  if ((st = record(ev, 5, s))) return st;
+  return dbg ? launch_guards(a, L, false, s) : MOE_OK;
 }
 
 }  // namespace
@@ -542,6 +598,24 @@ int moe_fp8_device_error(const MoeFwdArgs* a, void* stream, int32_t* code, int32
   return MOE_OK;
 }
 
+int moe_fp8_check_workspace(const MoeFwdArgs* a, void* stream) {
+  if (!a) return MOE_ERR_INVALID_ARG;
+  int st = validate_shape(a);
+  if (st) return st;
+  const Layout L = make_layout(a);
+  if (a->T == 0) return MOE_OK;
+  if (!a->workspace || a->workspace_bytes < L.w.total_bytes) return MOE_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return MOE_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev))) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CtrlBlock* ctrl = ws_ptr<CtrlBlock>(a, L.w.ctrl);
+  // error and error_info are adjacent words
+  if (cudaMemsetAsync(&ctrl->error, 0, 2 * sizeof(int), s) != cudaSuccess) return MOE_ERR_CUDA;
+  if ((st = launch_check_dispatch(a, L, dev->sms, s))) return st;
+  return debug_checks(a) ? launch_guards(a, L, false, s) : MOE_OK;
+}
+
 const char* moe_fp8_status_string(int code) {
   switch (code) {
     case MOE_OK: return "ok";
@@ -553,6 +627,7 @@ const char* moe_fp8_status_string(int code) {
     case MOE_ERR_TIMEOUT: return "device-side wait timed out";
     case MOE_ERR_DEVICE: return "device is not sm_100 (B200)";
     case MOE_ERR_TOO_LARGE: return "size exceeds the fixed scratch of moe_fp8_route_noalloc";
+    case MOE_ERR_BOUNDS: return "a debug check of the dispatch tables or workspace guards failed";
     default: return "unknown status";
   }
 }

@@ -120,6 +120,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);   // [1]: wait limit
   int* tstart_s = reinterpret_cast<int*>(tmem_slot + 3);
   int* counts_s = tstart_s + kMaxExperts + 1;
+  int* skip_s = counts_s + kMaxExperts;   // debug checks failed: no units
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.E_local, NT = p.n_tiles, KB = p.num_k_blocks;
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(never, 1);
     abort_flag[0] = 0;
     abort_flag[1] = static_cast<int>(p.wait_limit_us);
+    *skip_s = p.skip_on_error && *reinterpret_cast<volatile const int*>(&p.ctrl->error) != 0;
     fence_barrier_init();
   }
   if (warp == 9) {
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int total_units = tstart_s[E] * NT;
+  const int total_units = *skip_s ? 0 : tstart_s[E] * NT;
 
   if (warp >= 8) {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));

@@ -189,6 +189,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   int* ustart_s = reinterpret_cast<int*>(red_s + 4 * kSmallN);
   int* counts_s = ustart_s + kMaxExperts + 1;
   int* tstart_s = counts_s + kMaxExperts;
+  int* skip_s = tstart_s + kMaxExperts;   // debug checks failed: no units
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.E_local, NT = p.n_tiles, KB = p.num_k_blocks;
@@ -230,6 +231,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     counts_s[i] = p.counts[i];
     tstart_s[i] = p.tile_start[i];
   }
+  if (threadIdx.x == 0)
+    *skip_s = p.skip_on_error && *reinterpret_cast<volatile const int*>(&p.ctrl->error) != 0;
   __syncthreads();
   if (warp == 0) {
     // Unit prefix over experts: NT x ceil(count / 16) units each, warp scan
@@ -261,7 +264,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int total_units = ustart_s[E];
+  const int total_units = *skip_s ? 0 : ustart_s[E];
   // Split units add partial products, which the deterministic combine's
   // stored rows cannot take.
   const SegSpace segs = make_seg_space(total_units, KB, kMode == kGemm2 && p.rows_out == nullptr);

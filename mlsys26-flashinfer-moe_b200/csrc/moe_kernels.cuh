@@ -98,8 +98,39 @@ struct GemmParams {
                               // intermediate (bf16(code * scale)) instead of codes + scales
   unsigned int wait_limit_us;         // bound of the bounded waits (wait_limit_us())
   int stall;               // GEMM1, failure-detection tests: first MMA issuer waits forever
+  int skip_on_error;       // MOE_FLAG_DEBUG: no units when the control block holds an error
   CtrlBlock* ctrl;
 };
+
+// Debug checks (moe_check.cu).  Guards are 16-byte patterns written after the
+// workspace buffers; `guard` holds their byte offsets from `base`.
+constexpr int kMaxGuards = 24;
+constexpr int kGuardBytes = 16;
+struct GuardList {
+  uint8_t* base;
+  int n;
+  size_t off[kMaxGuards];
+};
+
+struct CheckParams {
+  int T, top_k, E_global, E_local, local_expert_offset;
+  int64_t npad;
+  const int* counts;
+  const int* tile_start;
+  const int* topk_idx;
+  const float* topk_weights;
+  const int* row_token;
+  const float* row_weight;
+  const int* assign_row;
+  CtrlBlock* ctrl;
+};
+
+// MOE_CHECK_* checks of the routing and dispatch tables; reports the first
+// failure as MOE_ERR_BOUNDS.
+__global__ void moe_check_dispatch_kernel(CheckParams p);
+// write != 0: stores the pattern into every guard; else reports the first
+// guard that differs from it (MOE_CHECK_GUARD, index = guard number).
+__global__ void moe_guard_kernel(GuardList g, int write, CtrlBlock* ctrl);
 
 __global__ void moe_route_kernel(RouteParams p);
 __global__ void moe_permute_kernel(PermuteParams p);

@@ -64,7 +64,10 @@ __device__ __forceinline__ void route_one_token(const RouteParams& p, int t, int
 #pragma unroll
   for (int j = 0; j < EPL; ++j) {
     s[j] = sigmoid_f32(x[j]);
-    sb[j] = active ? s[j] + bias[j] : -INFINITY;
+    const float v = s[j] + bias[j];
+    // A NaN score (NaN logit or bias) ranks below every number, so the
+    // comparisons below stay a total order.
+    sb[j] = active && !isnan(v) ? v : -INFINITY;
   }
   // --- group score: sum of the two largest sb in the group (kernel.py:479-488)
   float m1 = -INFINITY, m2 = -INFINITY;
@@ -93,39 +96,40 @@ __device__ __forceinline__ void route_one_token(const RouteParams& p, int t, int
     better += (o > gscore) || (o == gscore && g < my_group);
   }
   const bool keep = active && better < p.topk_group;
-  float cand[EPL];
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) cand[j] = keep ? sb[j] : -INFINITY;
   // --- top_k experts by sb, ties to the lowest expert id (522-534).  Each
-  // round: the lane's best candidate (first of equal values, so its lowest
-  // expert), the warp maximum of an order-preserving integer key in one
-  // redux, and the lowest lane holding it -- lane l owns experts
+  // round: the lane's best candidate not yet taken (first of equal values, so
+  // its lowest expert), the warp maximum of an order-preserving integer key in
+  // one redux, and the lowest lane holding it -- lane l owns experts
   // [l*EPL, (l+1)*EPL), so that lane's candidate is the lowest expert id
-  // among the equal maxima, as in the reference's max-and-mask.
+  // among the equal maxima, as in the reference's max-and-mask.  Taken
+  // experts are tracked apart from their scores, so even -inf scores (from
+  // -inf biases or NaN inputs) can never be picked twice: the kept groups hold
+  // at least top_k experts, so every round finds an untaken one, and a token's
+  // experts are always distinct (the permute relies on it).
+  unsigned taken = keep ? 0u : (1u << EPL) - 1u;   // lanes of dropped groups offer none
   int my_idx = 0;
   float my_s = 0.f;
   for (int k = 0; k < p.top_k; ++k) {
     float bv = -INFINITY;
-    int bj = 0;
+    int bj = -1;
 #pragma unroll
     for (int j = 0; j < EPL; ++j) {
-      if (cand[j] > bv) {
-        bv = cand[j];
+      if (!((taken >> j) & 1u) && (bj < 0 || sb[j] > bv)) {
+        bv = sb[j];
         bj = j;
       }
     }
-    const unsigned key = ordered_key(bv);
+    // ordered_key(-inf) = 0x007fffff, above the 0 of a lane with nothing left
+    const unsigned key = bj < 0 ? 0u : ordered_key(bv);
     const unsigned kmax = __reduce_max_sync(full, key);
     const int src = __ffs(__ballot_sync(full, key == kmax)) - 1;
+    bj = max(bj, 0);
     float sv = 0.f;
     if (lane == src) {
+      taken |= 1u << bj;
 #pragma unroll
-      for (int j = 0; j < EPL; ++j) {
-        if (j == bj) {
-          sv = s[j];
-          cand[j] = -INFINITY;
-        }
-      }
+      for (int j = 0; j < EPL; ++j)
+        if (j == bj) sv = s[j];
     }
     const int bi = __shfl_sync(full, e0 + bj, src);
     sv = __shfl_sync(full, sv, src);

@@ -22,14 +22,20 @@ MOE_ERR_CUDA = -5
 MOE_ERR_TIMEOUT = -6
 MOE_ERR_DEVICE = -7
 MOE_ERR_TOO_LARGE = -8
+MOE_ERR_BOUNDS = -9
 
 MOE_PROFILE_EVENTS = 6
+
+# What failed, in bits 24-31 of the info word of MOE_ERR_BOUNDS.
+CHECK_SITES = {1: "counts", 2: "tile_start", 3: "topk_idx", 4: "topk_weights", 5: "row_token",
+               6: "row_weight", 7: "row_expert", 8: "assign_row", 9: "guard"}
 
 MOE_BIAS_F32 = 0
 MOE_BIAS_BF16 = 1
 MOE_BIAS_F16 = 2
 
 MOE_FLAG_DETERMINISTIC = 0x1
+MOE_FLAG_DEBUG = 0x2
 MOE_FLAG_TEST_STALL = 0x100
 
 
@@ -110,6 +116,7 @@ SYMBOLS = {
     "moe_fp8_device_error": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p,
                                             ctypes.POINTER(ctypes.c_int32),
                                             ctypes.POINTER(ctypes.c_int32)]),
+    "moe_fp8_check_workspace": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p]),
     "moe_fp8_route_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,

@@ -60,14 +60,17 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                local_expert_offset: int, routed_scaling_factor: float, output: torch.Tensor,
                n_group: int = 8, topk_group: int = 4, top_k: int = 8,
-               deterministic: bool = False, gemm2_weights_bf16: Optional[torch.Tensor] = None):
+               deterministic: bool = False, gemm2_weights_bf16: Optional[torch.Tensor] = None,
+               debug: bool = False):
     """Validate like the reference and fill a ``MoeFwdArgs`` (no workspace yet).
 
     ``deterministic`` selects the fixed-order combine (``MOE_FLAG_DETERMINISTIC``):
     bit-identical output from run to run, at the cost of one fp32 row per
     (token, expert) assignment in the workspace.  ``gemm2_weights_bf16``: the
     same down-projection weights prepared by ``prepare_gemm2_weights`` (bf16
-    GEMM2 without block-scale promotion on the prefill path).
+    GEMM2 without block-scale promotion on the prefill path).  ``debug`` sets
+    ``MOE_FLAG_DEBUG`` (device checks of the dispatch tables and workspace
+    guards).
 
     Returns ``(args, keepalive, out_dev)``: ``keepalive`` holds the device
     copies the pointers refer to; ``out_dev`` is where the kernel writes (the
@@ -120,7 +123,8 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     a.n_group, a.topk_group, a.top_k = int(n_group), int(topk_group), int(top_k)
     a.routed_scaling_factor = float(routed_scaling_factor)
     a.bias_dtype = _BIAS_DTYPES[routing_bias.dtype]
-    a.flags = _lib.MOE_FLAG_DETERMINISTIC if deterministic else 0
+    a.flags = (_lib.MOE_FLAG_DETERMINISTIC if deterministic else 0) | \
+        (_lib.MOE_FLAG_DEBUG if debug else 0)
     if gemm2_weights_bf16 is not None:
         assert gemm2_weights_bf16.dtype == torch.bfloat16 and \
             gemm2_weights_bf16.shape == (e_local, h, i), \
@@ -177,7 +181,7 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
         routed_scaling_factor: float, output: torch.Tensor, *, n_group: int = 8,
         topk_group: int = 4, top_k: int = 8, workspace: Optional[torch.Tensor] = None,
         deterministic: bool = False,
-        gemm2_weights_bf16: Optional[torch.Tensor] = None) -> None:
+        gemm2_weights_bf16: Optional[torch.Tensor] = None, debug: bool = False) -> None:
     """Fused FP8 block-scale DeepSeek-V3 MoE forward (reference ``kernel.py:562``).
 
     Writes the bf16 ``[T, H]`` layer output into ``output``.  Only the experts
@@ -188,16 +192,21 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     fp32 atomics as the reference does (kernel.py:246-250).
     ``gemm2_weights_bf16`` (from ``prepare_gemm2_weights(gemm2_weights,
     gemm2_weights_scale)``, made once for a layer's weights) runs the prefill
-    GEMM2 on bf16 operands; decode-sized batches ignore it.
+    GEMM2 on bf16 operands; decode-sized batches ignore it.  ``debug=True``
+    checks the routing and dispatch tables on the device before the GEMMs use
+    them and guards every workspace buffer; it then waits for the forward and
+    raises ``MoeError`` (a ``RuntimeError``) naming the failed check.
     """
     args, keep, out_dev = build_args(routing_logits, routing_bias, hidden_states,
                                      hidden_states_scale, gemm1_weights, gemm1_weights_scale,
                                      gemm2_weights, gemm2_weights_scale, local_expert_offset,
                                      routed_scaling_factor, output, n_group, topk_group, top_k,
-                                     deterministic, gemm2_weights_bf16)
+                                     deterministic, gemm2_weights_bf16, debug)
     device = keep[0].device
     if args.T > 0:
         forward_args(args, workspace, device)
+        if debug:
+            raise_device_error(args, "moe_fp8_forward (debug)")
     if out_dev is not output:
         output.copy_(out_dev)
     return None
@@ -261,6 +270,40 @@ def device_error(args: _lib.MoeFwdArgs, stream: Optional[torch.cuda.Stream] = No
     if st:
         _raise(st, "moe_fp8_device_error")
     return code.value, info.value
+
+
+def describe_error(code: int, info: int) -> str:
+    """Text for a device error word: the failed check and index of
+    ``MOE_ERR_BOUNDS``, the wait site of ``MOE_ERR_TIMEOUT``."""
+    if code == _lib.MOE_ERR_BOUNDS:
+        site = _lib.CHECK_SITES.get((info >> 24) & 0xFF, "unknown")
+        return f"{_lib.status_string(code)}: check '{site}' at index {info & 0xFFFFFF}"
+    if code == _lib.MOE_ERR_TIMEOUT:
+        return f"{_lib.status_string(code)} at wait site {info}"
+    return f"{_lib.status_string(code)} (info {info})"
+
+
+def raise_device_error(args: _lib.MoeFwdArgs, where: str,
+                       stream: Optional[torch.cuda.Stream] = None) -> None:
+    """Waits for the stream and raises ``MoeError`` if the device error word
+    of the workspace in ``args`` is set."""
+    code, info = device_error(args, stream)
+    if code:
+        err = _lib.MoeError(code, where)
+        err.args = (f"{where}: {describe_error(code, info)}",)
+        err.info = info
+        raise err
+
+
+def check_workspace(args: _lib.MoeFwdArgs, stream: Optional[torch.cuda.Stream] = None):
+    """Runs ``moe_fp8_check_workspace`` on the tables the last forward left
+    in ``args.workspace`` (and its guards when ``args.flags`` has
+    ``MOE_FLAG_DEBUG``); returns the resulting (code, info)."""
+    stream = stream or torch.cuda.current_stream()
+    st = _lib.load().moe_fp8_check_workspace(ctypes.byref(args), ctypes.c_void_p(stream.cuda_stream))
+    if st:
+        _raise(st, "moe_fp8_check_workspace")
+    return device_error(args, stream)
 
 
 def workspace_views(args: _lib.MoeFwdArgs, workspace: torch.Tensor) -> dict:

@@ -116,6 +116,40 @@ def test_forward_argument_errors_need_no_gpu():
     assert lib.moe_fp8_forward(ctypes.byref(a), None) == _lib.MOE_ERR_INVALID_ARG
 
 
+def test_check_workspace_argument_errors_need_no_gpu():
+    lib = _lib.load()
+    assert lib.moe_fp8_check_workspace(None, None) == _lib.MOE_ERR_INVALID_ARG
+    a0 = _args(T=0)
+    assert lib.moe_fp8_check_workspace(ctypes.byref(a0), None) == _lib.MOE_OK
+    a = _args(T=4)
+    assert lib.moe_fp8_check_workspace(ctypes.byref(a), None) == _lib.MOE_ERR_WORKSPACE
+    a.flags = _lib.MOE_FLAG_DEBUG | _lib.MOE_FLAG_DETERMINISTIC
+    assert lib.moe_fp8_workspace_size(ctypes.byref(a), ctypes.byref(ctypes.c_size_t())) == 0
+    a.flags = 0x40
+    assert lib.moe_fp8_check_workspace(ctypes.byref(a), None) == _lib.MOE_ERR_INVALID_ARG
+
+
+def test_every_buffer_leaves_room_for_its_guard():
+    """16 guard bytes fit between each buffer's end and the next buffer."""
+    t, k, h, i, el = 300, 8, 7168, 2048, 256
+    a = _args(T=t)
+    a.flags = _lib.MOE_FLAG_DETERMINISTIC
+    lay = _lib.MoeWorkspaceLayout()
+    assert _lib.load().moe_fp8_workspace_layout(ctypes.byref(a), ctypes.byref(lay)) == 0
+    npad = lay.npad
+    sizes = dict(topk_idx=4 * t * k, topk_weights=4 * t * k, counts=4 * el,
+                 tile_start=4 * (el + 1), row_token=4 * npad, row_weight=4 * npad,
+                 a_perm=npad * h, a_scale_perm=4 * (h // 128) * npad, inter=npad * i,
+                 inter_scale=4 * (i // 64) * npad, out_f32=4 * t * h, assign_row=4 * t * k,
+                 rows_out=4 * npad * h)
+    names = [f for f, _ in _lib.MoeWorkspaceLayout._fields_[4:]]
+    offs = [getattr(lay, f) for f in names] + [lay.total_bytes]
+    for n, (f, o) in enumerate(zip(names, offs)):
+        if f in sizes:
+            guard = (o + sizes[f] + 15) // 16 * 16
+            assert guard + 16 <= offs[n + 1], f
+
+
 def test_status_strings():
-    for code in (0, -1, -2, -3, -4, -5, -6, -7):
+    for code in (0, -1, -2, -3, -4, -5, -6, -7, -8, -9):
         assert _lib.status_string(code) != "unknown status"
