@@ -238,6 +238,23 @@ int moe_fp8_route_noalloc(const float* routing_logits, const void* routing_bias,
 int moe_fp8_prepare_gemm2_bf16(const void* w2, const float* w2_scale, int64_t E_local, int64_t H,
                                int64_t I, void* out, void* stream);
 
+/* Router logits, the producer of routing_logits (DeepSeek-V3's gate):
+ * logits[T, E] = x[T, H] . w_gate[E, H]^T with bf16 x and w_gate (row-major),
+ * products exact in fp32 and fp32 accumulation, fp32 logits [T, E].  The
+ * reference receives the logits as an input (kernel.py:562); this op is the
+ * step before it (SURVEY's router-GEMM neighbour), with no counterpart there.
+ * Batches of at most 128 tokens, and shapes with E not a multiple of 256 or H
+ * not a multiple of 64, run on CUDA cores in a fixed summation order with every
+ * addition rounded to nearest (no workspace needed: pass NULL, 0); larger
+ * batches run on the tensor cores (tcgen05 kind::f16, whose fp32 accumulator
+ * does not round each addition to nearest: about 1e-5 of the largest logit at
+ * H=7168) and need moe_router_workspace_size bytes of workspace (256-byte
+ * aligned).  Both paths give the same bits on every run.  H must be a multiple of 8; x, w_gate and logits 16-byte
+ * aligned; T < 2^24, E <= 65536.  Asynchronous on `stream`, no allocation. */
+int moe_router_workspace_size(int64_t T, int64_t H, int64_t E, size_t* bytes);
+int moe_router_logits_bf16(const void* x, const void* w_gate, int64_t T, int64_t H, int64_t E,
+                           float* logits, void* workspace, size_t workspace_bytes, void* stream);
+
 /* bf16 -> FP8 e4m3 quantisation of activations with one fp32 scale per token
  * and 128 columns: x [T, H] bf16 (row-major) -> q [T, H] e4m3 and
  * scale [H/128, T] fp32, scale = max(amax * fp32(1/448), 1e-12),

@@ -25,7 +25,7 @@ LIB = os.path.join(OUT_DIR, "libmoe_b200.so")
 OBJ_DIR = os.path.join(HERE, "_build")
 
 SOURCES = ["moe_api.cu", "moe_route.cu", "moe_gemm.cu", "moe_gemm_small.cu", "moe_quant.cu", "moe_ep.cu",
-           "moe_check.cu"]
+           "moe_check.cu", "moe_router.cu"]
 HEADERS = ["moe_common.cuh", "moe_kernels.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

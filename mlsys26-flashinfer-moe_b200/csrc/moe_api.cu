@@ -530,6 +530,47 @@ int num_sms(int* out) {
 
 MoeWorkspaceLayout workspace_layout_for(const MoeFwdArgs* a) { return make_layout(a).w; }
 
+// ---------------------------------------------------------------------------
+// router logits
+// ---------------------------------------------------------------------------
+namespace {
+
+bool router_shape_ok(int64_t T, int64_t H, int64_t E) {
+  return T >= 0 && T < (int64_t(1) << 24) && H >= 8 && H % 8 == 0 && H <= 65536 && E >= 1 &&
+         E <= 65536;
+}
+
+// The tensor-core path: a batch big enough to fill row tiles, E in whole
+// 256-column tiles, H in whole 128-byte (64-element) K blocks.
+bool router_uses_tc(int64_t T, int64_t H, int64_t E) {
+  return T > kRouterGemvMaxTokens && E % kTileN == 0 && H % 64 == 0;
+}
+
+struct RouterLayout {
+  int64_t npad;
+  size_t ctrl, tile_start, counts, row_token, row_weight, total;
+};
+
+RouterLayout router_layout(int64_t T) {
+  RouterLayout r{};
+  r.npad = (T + kTileM - 1) / kTileM * kTileM;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  r.ctrl = take(sizeof(CtrlBlock));
+  r.tile_start = take(2 * sizeof(int));
+  r.counts = take(sizeof(int));
+  r.row_token = take(sizeof(int) * r.npad);
+  r.row_weight = take(sizeof(float) * r.npad);
+  r.total = off;
+  return r;
+}
+
+}  // namespace
+
 }  // namespace moe
 
 using namespace moe;
@@ -643,6 +684,66 @@ int moe_fp8_prepare_gemm2_bf16(const void* w2, const float* w2_scale, int64_t E_
   if (st) return st;
   return launch_prepare_w2_bf16(w2, w2_scale, E_local, H, I, out, dev->sms,
                                 static_cast<cudaStream_t>(stream));
+}
+
+int moe_router_workspace_size(int64_t T, int64_t H, int64_t E, size_t* bytes) {
+  if (!bytes) return MOE_ERR_INVALID_ARG;
+  if (!router_shape_ok(T, H, E)) return MOE_ERR_SHAPE;
+  *bytes = router_uses_tc(T, H, E) ? router_layout(T).total : 0;
+  return MOE_OK;
+}
+
+int moe_router_logits_bf16(const void* x, const void* w_gate, int64_t T, int64_t H, int64_t E,
+                           float* logits, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!router_shape_ok(T, H, E)) return MOE_ERR_SHAPE;
+  if (T == 0) return MOE_OK;
+  if (!x || !w_gate || !logits) return MOE_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w_gate) || !aligned16(logits)) return MOE_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  int st = device_info(&dev);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w_gate);
+  if (!router_uses_tc(T, H, E)) {
+    return launch_router_gemv(xb, wb, T, H, E, logits, s);
+  }
+  const RouterLayout L = router_layout(T);
+  if (!workspace || workspace_bytes < L.total) return MOE_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MOE_ERR_ALIGNMENT;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* tile_start = reinterpret_cast<int*>(ws + L.tile_start);
+  int* counts = reinterpret_cast<int*>(ws + L.counts);
+  int* row_token = reinterpret_cast<int*>(ws + L.row_token);
+  float* row_weight = reinterpret_cast<float*>(ws + L.row_weight);
+  CtrlBlock* ctrl = reinterpret_cast<CtrlBlock*>(ws + L.ctrl);
+  int64_t sblocks = (L.npad + 255) / 256;
+  if (sblocks > dev->sms) sblocks = dev->sms;
+  moe_router_setup_kernel<<<static_cast<int>(sblocks), 256, 0, s>>>(
+      static_cast<int>(T), static_cast<int>(L.npad), tile_start, counts, row_token, row_weight,
+      ctrl);
+  if (cudaGetLastError() != cudaSuccess) return MOE_ERR_CUDA;
+  GemmParams g{};
+  g.tile_start = tile_start;
+  g.counts = counts;
+  g.row_token = row_token;
+  g.row_weight = row_weight;
+  g.ctrl = ctrl;
+  // One "expert" whose 128-row tiles are the tokens in order and whose weight
+  // rows are the E router rows; bf16 matrices read as byte matrices, so a
+  // 128-byte K block holds 64 elements.
+  CUtensorMap tm_a, tm_b;
+  if ((st = byte_tile_map(x, 2 * H, T, &tm_a))) return st;
+  if ((st = byte_tile_map(w_gate, 2 * H, E, &tm_b))) return st;
+  g.E_local = 1;
+  g.num_k_blocks = static_cast<int>(2 * H / kBlockK);
+  g.n_tiles = static_cast<int>(E / kTileN);
+  g.b_rows_per_expert = static_cast<int>(E);
+  g.hidden = static_cast<int>(E);   // width of the stored rows
+  g.npad = L.npad;
+  g.rows_out = logits;              // row r of the single "expert" = token r
+  g.wait_limit_us = wait_limit_us(0);
+  return launch_gemm(kGemm2Bf16, tm_a, tm_b, g, dev->sms, s);
 }
 
 int moe_bf16_to_fp8_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale,

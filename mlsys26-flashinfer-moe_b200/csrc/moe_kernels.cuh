@@ -102,6 +102,22 @@ struct GemmParams {
   CtrlBlock* ctrl;
 };
 
+// Router logits (moe_router.cu).  Batches up to kRouterGemvMaxTokens tokens,
+// and shapes outside the tensor-core path (E a multiple of 256, H of 64), take
+// the CUDA-core kernel: a block per kRouterRows experts x kRouterGemvTokens
+// tokens, each token row loaded once for the block's experts.  Above
+// kRouterGemvMaxTokens the tensor-core path is faster (it streams the gate
+// weight once per 128 tokens).  Measured alternatives (1 or 2 experts a block,
+// 16 or 32 warps, unrolled loads) were no faster at T <= 8, where the launch
+// dominates, and up to 3x slower at T = 64-256.
+constexpr int kRouterRows = 4;
+constexpr int kRouterGemvTokens = 8;
+constexpr int64_t kRouterGemvMaxTokens = 128;
+int launch_router_gemv(const __nv_bfloat16* x, const __nv_bfloat16* w, int64_t T, int64_t H,
+                       int64_t E, float* out, cudaStream_t s);
+__global__ void moe_router_setup_kernel(int T, int npad, int* tile_start, int* counts,
+                                        int* row_token, float* row_weight, CtrlBlock* ctrl);
+
 // Debug checks (moe_check.cu).  Guards are 16-byte patterns written after the
 // workspace buffers; `guard` holds their byte offsets from `base`.
 constexpr int kMaxGuards = 24;

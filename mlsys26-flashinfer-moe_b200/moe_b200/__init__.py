@@ -6,10 +6,10 @@
 """
 from .api import (run, build_args, forward_args, workspace_views, device_error,  # noqa: F401
                   quantize_1x128, prepare_gemm2_weights, check_workspace, describe_error,
-                  raise_device_error)
+                  raise_device_error, router_logits)
 from .graph import LayerGraph  # noqa: F401
 from . import workloads  # noqa: F401
 
 __all__ = ["run", "build_args", "forward_args", "workspace_views", "device_error", "quantize_1x128",
            "prepare_gemm2_weights", "check_workspace", "describe_error", "raise_device_error",
-           "LayerGraph", "workloads"]
+           "router_logits", "LayerGraph", "workloads"]

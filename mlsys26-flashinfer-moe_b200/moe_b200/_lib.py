@@ -116,6 +116,10 @@ SYMBOLS = {
     "moe_fp8_device_error": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p,
                                             ctypes.POINTER(ctypes.c_int32),
                                             ctypes.POINTER(ctypes.c_int32)]),
+    "moe_router_workspace_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                 ctypes.POINTER(ctypes.c_size_t)]),
+    "moe_router_logits_bf16": (ctypes.c_int, [_VP, _VP, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int64, _VP, _VP, ctypes.c_size_t, _VP]),
     "moe_fp8_check_workspace": (ctypes.c_int, [ctypes.POINTER(MoeFwdArgs), ctypes.c_void_p]),
     "moe_fp8_route_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,

@@ -235,6 +235,48 @@ def prepare_gemm2_weights(gemm2_weights: torch.Tensor, gemm2_weights_scale: torc
     return out
 
 
+_router_ws: dict = {}
+
+
+def router_logits(x: torch.Tensor, w_gate: torch.Tensor, out: Optional[torch.Tensor] = None,
+                  workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Router logits ``x @ w_gate.T`` for bf16 ``x [T, H]`` and ``w_gate [E, H]`` (CUDA),
+    fp32 ``[T, E]`` on the current stream: the ``routing_logits`` input of ``run()``.
+    Products of the bf16 values are exact in fp32 and summed in fp32; large
+    batches run on the tensor cores and use ``workspace`` (an internal cached
+    buffer per stream when omitted)."""
+    assert x.dtype == torch.bfloat16 and x.dim() == 2, "x must be a bf16 [T, H] tensor"
+    assert w_gate.dtype == torch.bfloat16 and w_gate.dim() == 2, "w_gate must be a bf16 [E, H] tensor"
+    assert x.is_cuda and w_gate.is_cuda, "x and w_gate must be CUDA tensors"
+    t, h = (int(v) for v in x.shape)
+    e = int(w_gate.shape[0])
+    assert int(w_gate.shape[1]) == h, f"w_gate must be [E, {h}]"
+    x, w_gate = x.contiguous(), w_gate.contiguous()
+    if out is None:
+        out = torch.empty(t, e, dtype=torch.float32, device=x.device)
+    assert out.shape == (t, e) and out.dtype == torch.float32 and out.is_contiguous()
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    code = lib.moe_router_workspace_size(t, h, e, ctypes.byref(nbytes))
+    if code:
+        _raise(code, "moe_router_workspace_size")
+    stream = torch.cuda.current_stream(x.device)
+    ws_ptr, ws_bytes = None, 0
+    if nbytes.value:
+        if workspace is None:
+            key = (x.device.index, stream.cuda_stream)
+            workspace = _router_ws.get(key)
+            if workspace is None or workspace.numel() < nbytes.value:
+                workspace = torch.empty(nbytes.value, dtype=torch.uint8, device=x.device)
+                _router_ws[key] = workspace
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel()
+    code = lib.moe_router_logits_bf16(x.data_ptr(), w_gate.data_ptr(), t, h, e, out.data_ptr(),
+                                      ws_ptr, ws_bytes, ctypes.c_void_p(stream.cuda_stream))
+    if code:
+        _raise(code, "moe_router_logits_bf16")
+    return out
+
+
 def quantize_1x128(x: torch.Tensor, q: Optional[torch.Tensor] = None,
                    scale: Optional[torch.Tensor] = None):
     """bf16 ``[T, H]`` CUDA activations -> (e4m3 ``[T, H]``, fp32 ``[H/128, T]``) on the

@@ -150,6 +150,19 @@ def test_every_buffer_leaves_room_for_its_guard():
             assert guard + 16 <= offs[n + 1], f
 
 
+def test_router_argument_errors_need_no_gpu():
+    lib = _lib.load()
+    n = ctypes.c_size_t(0)
+    assert lib.moe_router_workspace_size(8192, 7168, 256, ctypes.byref(n)) == 0 and n.value > 0
+    assert lib.moe_router_workspace_size(128, 7168, 256, ctypes.byref(n)) == 0 and n.value == 0
+    assert lib.moe_router_workspace_size(8192, 7168, 16, ctypes.byref(n)) == 0 and n.value == 0
+    assert lib.moe_router_workspace_size(8, 7167, 256, ctypes.byref(n)) == _lib.MOE_ERR_SHAPE
+    assert lib.moe_router_workspace_size(-1, 7168, 256, ctypes.byref(n)) == _lib.MOE_ERR_SHAPE
+    assert lib.moe_router_logits_bf16(None, None, 0, 7168, 256, None, None, 0, None) == _lib.MOE_OK
+    assert lib.moe_router_logits_bf16(None, None, 4, 7168, 256, None, None, 0,
+                                      None) == _lib.MOE_ERR_INVALID_ARG
+
+
 def test_status_strings():
     for code in (0, -1, -2, -3, -4, -5, -6, -7, -8, -9):
         assert _lib.status_string(code) != "unknown status"
