@@ -111,6 +111,17 @@ typedef struct MoeFwdArgs {
    * prefill path run GEMM2 on bf16 operands without block-scale promotion
    * (GEMM1 then writes the dequantised intermediate); NULL = FP8 path. */
   const void* gemm2_weights_bf16;
+  /* Shared experts (0 or 1; DeepSeek-V3 has one, intermediate size I).  When 1,
+   * the weight tensors hold E_local + 1 experts: the routed experts
+   * [local_expert_offset, local_expert_offset + E_local) followed by the shared
+   * expert, i.e. gemm1_weights [E_local + 1, 2I, H], gemm2_weights
+   * [E_local + 1, H, I] and their scales likewise.  Every token also goes
+   * through the shared expert with weight 1, summed into the same output as
+   * its routed experts (y = sum_k w_k E_k(x) + S(x)).  The reference has no
+   * shared expert (kernel.py:562 computes the routed sum only); callers that
+   * run it separately add it afterwards.  Not combined with
+   * gemm2_weights_bf16. */
+  int64_t n_shared_experts;
 } MoeFwdArgs;
 
 /* Offsets (bytes from the workspace base) of the per-stage buffers a forward
@@ -125,8 +136,9 @@ typedef struct MoeWorkspaceLayout {
   size_t topk_idx;         /* [T, top_k] int32   routed global expert ids, selection order */
   size_t topk_weights;     /* [T, top_k] fp32    routing weights */
   size_t block_base;       /* [route_blocks, E_local] int32 per-block bucket offsets */
-  size_t counts;           /* [E_local] int32    assignments per local expert */
-  size_t tile_start;       /* [E_local + 1] int32 prefix sum of 128-row tiles */
+  size_t counts;           /* [E_local + n_shared_experts] int32  rows per bucket (local
+                              experts, then the shared expert's T) */
+  size_t tile_start;       /* [E_local + n_shared_experts + 1] int32 prefix sum of 128-row tiles */
   size_t row_token;        /* [npad] int32       token of each permuted row */
   size_t row_weight;       /* [npad] fp32        routing weight of each permuted row */
   size_t a_perm;           /* [npad, H] e4m3     permuted hidden states */
@@ -178,13 +190,14 @@ int moe_fp8_device_error(const MoeFwdArgs* a, void* stream, int32_t* code, int32
 /* What failed, in bits 24-31 of the info word of MOE_ERR_BOUNDS; bits 0-23
  * hold the index of the failing element (expert, assignment t*top_k+k, row or
  * guard number). */
-#define MOE_CHECK_COUNTS 1       /* counts[e] outside [0, T] */
+#define MOE_CHECK_COUNTS 1       /* counts[e] outside [0, T] (the shared bucket's: not T) */
 #define MOE_CHECK_TILE_START 2   /* tile_start not the 128-row prefix of counts, or past npad */
 #define MOE_CHECK_TOPK_IDX 3     /* routed expert id outside [0, E_global) or repeated in a token */
 #define MOE_CHECK_TOPK_WEIGHT 4  /* routing weight not finite */
 #define MOE_CHECK_ROW_TOKEN 5    /* a live permuted row's token outside [0, T) */
 #define MOE_CHECK_ROW_WEIGHT 6   /* a live row's weight differs from its assignment's */
-#define MOE_CHECK_ROW_EXPERT 7   /* a live row's token was not routed to the row's expert */
+#define MOE_CHECK_ROW_EXPERT 7   /* a live row's token was not routed to the row's expert
+                                    (shared bucket: row i of the bucket is not token i) */
 #define MOE_CHECK_ASSIGN_ROW 8   /* an assignment's row is not the live row holding it */
 #define MOE_CHECK_GUARD 9        /* the guard after workspace buffer `index` was overwritten */
 

@@ -48,8 +48,13 @@ int validate_shape(const MoeFwdArgs* a) {
   if ((a->flags & ~(MOE_FLAG_DETERMINISTIC | MOE_FLAG_DEBUG | MOE_FLAG_TEST_STALL)) != 0 ||
       a->reserved != 0)
     return MOE_ERR_INVALID_ARG;
+  if (a->n_shared_experts < 0 || a->n_shared_experts > 1) return MOE_ERR_SHAPE;
+  if (a->n_shared_experts && a->gemm2_weights_bf16) return MOE_ERR_INVALID_ARG;
   return MOE_OK;
 }
+
+// Dispatch buckets: the local routed experts, then the shared expert if any.
+int64_t buckets(const MoeFwdArgs* a) { return a->E_local + a->n_shared_experts; }
 
 bool deterministic(const MoeFwdArgs* a) { return (a->flags & MOE_FLAG_DETERMINISTIC) != 0; }
 bool debug_checks(const MoeFwdArgs* a) { return (a->flags & MOE_FLAG_DEBUG) != 0; }
@@ -86,8 +91,11 @@ Layout make_layout(const MoeFwdArgs* a) {
   if (split > most) split = most;
   if (split < 1) split = 1;
   L.permute_split = static_cast<int>(split);
-  const int64_t nmax = T * (K < El ? K : El);
-  const int64_t active = El < nmax ? El : nmax;
+  // Rows: every local assignment plus, with a shared expert, every token once
+  // more; each non-empty bucket pads its last tile.
+  const int64_t ns = a->n_shared_experts, nb = El + ns;
+  const int64_t nmax = T * (K < El ? K : El) + ns * T;
+  const int64_t active = nb < nmax ? nb : nmax;
   int64_t tiles = (nmax + active * (kTileM - 1)) / kTileM;
   if (tiles < 1) tiles = 1;
   const int64_t npad = tiles * kTileM;
@@ -110,8 +118,8 @@ Layout make_layout(const MoeFwdArgs* a) {
   w.topk_idx = take(sizeof(int) * T * K);
   w.topk_weights = take(sizeof(float) * T * K);
   w.block_base = take(sizeof(int) * (L.blocks > 0 ? L.blocks : 1) * El);
-  w.counts = take(sizeof(int) * El);
-  w.tile_start = take(sizeof(int) * (El + 1));
+  w.counts = take(sizeof(int) * nb);
+  w.tile_start = take(sizeof(int) * (nb + 1));
   w.row_token = take(sizeof(int) * npad);
   w.row_weight = take(sizeof(float) * npad);
   w.a_perm = take(static_cast<size_t>(npad) * H);
@@ -276,6 +284,7 @@ RouteParams route_params(const MoeFwdArgs* a, const Layout& L, const int* T_dev)
   rp.tile_start = ws_ptr<int>(a, w.tile_start);
   rp.ctrl = ws_ptr<CtrlBlock>(a, w.ctrl);
   rp.T_dev = T_dev;
+  rp.n_shared = static_cast<int>(a->n_shared_experts);
   return rp;
 }
 
@@ -295,6 +304,7 @@ CheckParams check_params(const MoeFwdArgs* a, const Layout& L) {
   c.E_global = static_cast<int>(a->E_global);
   c.E_local = static_cast<int>(a->E_local);
   c.local_expert_offset = static_cast<int>(a->local_expert_offset);
+  c.n_shared = static_cast<int>(a->n_shared_experts);
   c.npad = w.npad;
   c.counts = ws_ptr<int>(a, w.counts);
   c.tile_start = ws_ptr<int>(a, w.tile_start);
@@ -309,7 +319,7 @@ CheckParams check_params(const MoeFwdArgs* a, const Layout& L) {
 
 int launch_check_dispatch(const MoeFwdArgs* a, const Layout& L, int sms, cudaStream_t s) {
   const CheckParams c = check_params(a, L);
-  const int64_t items = c.E_local + static_cast<int64_t>(c.T) * c.top_k + c.npad;
+  const int64_t items = c.E_local + c.n_shared + static_cast<int64_t>(c.T) * c.top_k + c.npad;
   int64_t blocks = (items + 255) / 256;
   if (blocks > 4 * sms) blocks = 4 * sms;
   moe_check_dispatch_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(c);
@@ -366,6 +376,7 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   // combine stores rows instead of adding into the accumulator)
   pp.zero_rows = det ? nullptr : out_f32;
   pp.assign_row = ws_ptr<int>(a, w.assign_row);
+  pp.n_shared = static_cast<int>(a->n_shared_experts);
   pp.row_token = ws_ptr<int>(a, w.row_token);
   pp.row_weight = ws_ptr<float>(a, w.row_weight);
   pp.a_perm = ws_ptr<uint8_t>(a, w.a_perm);
@@ -406,20 +417,21 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
   const uint32_t tok_box = small ? 16u : static_cast<uint32_t>(kTileM);
   CUtensorMap tm_a1, tm_b1, tm_a2, tm_b2;
   if ((st = byte_tile_map(pp.a_perm, H, w.npad, &tm_a1, tok_box))) return st;
-  if ((st = byte_tile_map(a->gemm1_weights, H, El * 2 * I, &tm_b1))) return st;
+  const int64_t nb = buckets(a);   // the shared expert's weights follow the routed experts'
+  if ((st = byte_tile_map(a->gemm1_weights, H, nb * 2 * I, &tm_b1))) return st;
   if (bf16_w2) {
     // bf16 matrices read as byte matrices: 128-byte boxes hold 64 elements of K.
     if ((st = byte_tile_map(ws_ptr<uint8_t>(a, w.inter_bf16), 2 * I, w.npad, &tm_a2))) return st;
-    if ((st = byte_tile_map(a->gemm2_weights_bf16, 2 * I, El * H, &tm_b2))) return st;
+    if ((st = byte_tile_map(a->gemm2_weights_bf16, 2 * I, nb * H, &tm_b2))) return st;
   } else {
     if ((st = byte_tile_map(ws_ptr<uint8_t>(a, w.inter), I, w.npad, &tm_a2, tok_box))) return st;
-    if ((st = byte_tile_map(a->gemm2_weights, I, El * H, &tm_b2))) return st;
+    if ((st = byte_tile_map(a->gemm2_weights, I, nb * H, &tm_b2))) return st;
   }
 
   GemmParams g1{};
   g1.tile_start = pp.tile_start;
   g1.counts = ws_ptr<int>(a, w.counts);
-  g1.E_local = static_cast<int>(El);
+  g1.E_local = static_cast<int>(nb);
   g1.num_k_blocks = static_cast<int>(H / kBlockK);
   g1.n_tiles = static_cast<int>(I / (kTileN / 2));
   g1.b_rows_per_expert = static_cast<int>(2 * I);
@@ -484,7 +496,9 @@ int launch_forward(const MoeFwdArgs* a, const Layout& L, cudaStream_t s,
                             static_cast<const float*>(g2.rows_out),
                             static_cast<const int*>(pp.assign_row),
                             static_cast<__nv_bfloat16*>(a->output), static_cast<int>(T),
-                            static_cast<int>(H), static_cast<int>(a->top_k));
+                            static_cast<int>(H), static_cast<int>(a->top_k),
+                            a->n_shared_experts ? static_cast<const int*>(pp.tile_start) + El
+                                                : static_cast<const int*>(nullptr));
   else
     e = launch_programmatic(moe_finalize_kernel, dim3(blocks), dim3(256), 0, s,
                             static_cast<const float*>(out_f32),

@@ -1,8 +1,9 @@
 // Debug checks of the forward's routing and dispatch tables and of the
 // workspace guards (MOE_FLAG_DEBUG, moe_fp8_check_workspace).
 //
-//   moe_check_dispatch_kernel  one thread per local expert, per (token, k)
-//                              assignment and per permuted row, grid-stride:
+//   moe_check_dispatch_kernel  one thread per dispatch bucket (local expert or
+//                              the shared expert), per (token, k) assignment
+//                              and per permuted row, grid-stride:
 //                              every index is range-checked before it is used
 //                              to read another table, so the kernel is safe on
 //                              any contents of the workspace.
@@ -25,7 +26,7 @@ __device__ __forceinline__ void fail(CtrlBlock* ctrl, int site, int64_t index) {
 
 __device__ __forceinline__ bool finite(float v) { return isfinite(v); }
 
-// Expert e of the local experts whose tile range [128*ts[e], 128*ts[e+1])
+// Bucket e of the E buckets whose tile range [128*ts[e], 128*ts[e+1])
 // holds row r, or -1.  The table is read at checked indices only, so a
 // corrupted (non-monotone) table yields a wrong expert or -1, never a read
 // outside it.
@@ -45,26 +46,28 @@ __device__ __forceinline__ int expert_of_row(const int* ts, int E, int64_t r) {
 
 __global__ void __launch_bounds__(256) moe_check_dispatch_kernel(CheckParams p) {
   const int64_t n_assign = static_cast<int64_t>(p.T) * p.top_k;
-  const int64_t total = p.E_local + n_assign + p.npad;
+  const int nb = p.E_local + p.n_shared;   // buckets: routed experts, then the shared expert
+  const int64_t total = nb + n_assign + p.npad;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += stride) {
-    if (i < p.E_local) {
-      // ---- per local expert: counts and the 128-row tile prefix
+    if (i < nb) {
+      // ---- per bucket: counts and the 128-row tile prefix (the shared
+      // expert's bucket holds every token)
       const int e = static_cast<int>(i);
       const int c = p.counts[e];
-      if (c < 0 || c > p.T) {
+      if (c < 0 || c > p.T || (e == p.E_local && c != p.T)) {
         fail(p.ctrl, MOE_CHECK_COUNTS, e);
         continue;
       }
       const int ts0 = p.tile_start[e], ts1 = p.tile_start[e + 1];
       if (e == 0 && ts0 != 0) fail(p.ctrl, MOE_CHECK_TILE_START, 0);
       if (ts1 - ts0 != (c + kTileM - 1) / kTileM) fail(p.ctrl, MOE_CHECK_TILE_START, e + 1);
-      if (e == p.E_local - 1 && (ts1 < 0 || static_cast<int64_t>(ts1) * kTileM > p.npad))
+      if (e == nb - 1 && (ts1 < 0 || static_cast<int64_t>(ts1) * kTileM > p.npad))
         fail(p.ctrl, MOE_CHECK_TILE_START, e + 1);
-    } else if (i < p.E_local + n_assign) {
+    } else if (i < nb + n_assign) {
       // ---- per assignment (token t, selection k)
-      const int64_t j = i - p.E_local;
+      const int64_t j = i - nb;
       const int t = static_cast<int>(j / p.top_k), k = static_cast<int>(j % p.top_k);
       const int idx = p.topk_idx[j];
       if (!finite(p.topk_weights[j])) fail(p.ctrl, MOE_CHECK_TOPK_WEIGHT, j);
@@ -89,14 +92,20 @@ __global__ void __launch_bounds__(256) moe_check_dispatch_kernel(CheckParams p) 
         fail(p.ctrl, MOE_CHECK_ASSIGN_ROW, j);
     } else {
       // ---- per permuted row: live rows hold an assignment of their expert
-      const int64_t r = i - p.E_local - n_assign;
-      const int e = expert_of_row(p.tile_start, p.E_local, r);
-      if (e < 0) continue;   // past the last expert's tiles
-      const int64_t live_end = static_cast<int64_t>(p.tile_start[e]) * kTileM + p.counts[e];
-      if (r >= live_end) continue;   // padding row of the expert's last tile
+      const int64_t r = i - nb - n_assign;
+      const int e = expert_of_row(p.tile_start, nb, r);
+      if (e < 0) continue;   // past the last bucket's tiles
+      const int64_t row0 = static_cast<int64_t>(p.tile_start[e]) * kTileM;
+      const int64_t live_end = row0 + p.counts[e];
+      if (r >= live_end) continue;   // padding row of the bucket's last tile
       const int tok = p.row_token[r];
       if (tok < 0 || tok >= p.T) {
         fail(p.ctrl, MOE_CHECK_ROW_TOKEN, r);
+        continue;
+      }
+      if (e == p.E_local) {   // shared expert: token r - row0, weight 1
+        if (tok != r - row0) fail(p.ctrl, MOE_CHECK_ROW_EXPERT, r);
+        if (p.row_weight[r] != 1.f) fail(p.ctrl, MOE_CHECK_ROW_WEIGHT, r);
         continue;
       }
       const int g = e + p.local_expert_offset;

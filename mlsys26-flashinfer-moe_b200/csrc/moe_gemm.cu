@@ -119,8 +119,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(never + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);   // [1]: wait limit
   int* tstart_s = reinterpret_cast<int*>(tmem_slot + 3);
-  int* counts_s = tstart_s + kMaxExperts + 1;
-  int* skip_s = counts_s + kMaxExperts;   // debug checks failed: no units
+  int* counts_s = tstart_s + kMaxBuckets + 1;
+  int* skip_s = counts_s + kMaxBuckets;   // debug checks failed: no units
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.E_local, NT = p.n_tiles, KB = p.num_k_blocks;

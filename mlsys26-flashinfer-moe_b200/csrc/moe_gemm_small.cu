@@ -65,7 +65,7 @@ struct SmallCfg {
 template <int kMode>
 constexpr int small_smem_bytes() {
   return 1024 + SmallCfg<kMode>::kStages * SmallCfg<kMode>::kStageBytes +
-         2 * kSmallScaleFloats * 4 + 4096 + (2 * kMaxExperts + 2) * 4;
+         2 * kSmallScaleFloats * 4 + 4096 + (2 * kMaxBuckets + 2) * 4;
 }
 
 struct SmallUnit {
@@ -187,9 +187,9 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);   // [1]: wait limit
   float* red_s = reinterpret_cast<float*>(tmem_slot + 4);     // [4][16] amax exchange
   int* ustart_s = reinterpret_cast<int*>(red_s + 4 * kSmallN);
-  int* counts_s = ustart_s + kMaxExperts + 1;
-  int* tstart_s = counts_s + kMaxExperts;
-  int* skip_s = tstart_s + kMaxExperts;   // debug checks failed: no units
+  int* counts_s = ustart_s + kMaxBuckets + 1;
+  int* tstart_s = counts_s + kMaxBuckets;
+  int* skip_s = tstart_s + kMaxBuckets;   // debug checks failed: no units
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.E_local, NT = p.n_tiles, KB = p.num_k_blocks;
@@ -235,13 +235,16 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     *skip_s = p.skip_on_error && *reinterpret_cast<volatile const int*>(&p.ctrl->error) != 0;
   __syncthreads();
   if (warp == 0) {
-    // Unit prefix over experts: NT x ceil(count / 16) units each, warp scan
-    // of up to 8 experts per lane.
-    int local[kMaxExperts / 32];
+    // Unit prefix over the buckets: NT x ceil(count / 16) units each, warp
+    // scan of kPerLane buckets per lane (32 * kPerLane > kMaxBuckets, so the
+    // lanes also cover index E, the total).
+    constexpr int kPerLane = (kMaxBuckets + 31) / 32;
+    static_assert(32 * kPerLane > kMaxBuckets, "the scan must reach index E");
+    int local[kPerLane];
     int sum = 0;
 #pragma unroll
-    for (int j = 0; j < kMaxExperts / 32; ++j) {
-      const int e = lane * (kMaxExperts / 32) + j;
+    for (int j = 0; j < kPerLane; ++j) {
+      const int e = lane * kPerLane + j;
       const int v = e < E ? NT * ((counts_s[e] + kSmallN - 1) / kSmallN) : 0;
       local[j] = sum;
       sum += v;
@@ -254,11 +257,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     }
     const int base = incl - sum;
 #pragma unroll
-    for (int j = 0; j < kMaxExperts / 32; ++j) {
-      const int e = lane * (kMaxExperts / 32) + j;
+    for (int j = 0; j < kPerLane; ++j) {
+      const int e = lane * kPerLane + j;
       if (e <= E) ustart_s[e] = base + local[j];
     }
-    if (lane == 31 && E == kMaxExperts) ustart_s[E] = incl;
   }
   tc_fence_before();
   __syncthreads();

@@ -7,6 +7,9 @@
 namespace moe {
 
 constexpr int kMaxExperts = 256;       // E_global (and hence E_local) limit
+// Dispatch buckets: the local routed experts plus at most one shared expert
+// (MoeFwdArgs.n_shared_experts), which is bucket E_local.
+constexpr int kMaxBuckets = kMaxExperts + 1;
 constexpr int kMaxTopK = 8;
 constexpr int kRouteThreads = 256;     // 8 warps, one token per warp at a time
 constexpr int kMaxTokensPerBlock = 256;
@@ -46,9 +49,10 @@ struct RouteParams {
   float* topk_weights;
   int* block_base;   // [blocks, E_local]
   int* counts;       // [E_local]
-  int* tile_start;   // [E_local + 1]
+  int* tile_start;   // [E_local + n_shared + 1]
   CtrlBlock* ctrl;
   const int* T_dev;  // when set, the number of rows is min(*T_dev, T) (expert-parallel receive side)
+  int n_shared;      // 1: bucket E_local holds every token (counts[E_local] = T)
 };
 
 struct PermuteParams {
@@ -68,6 +72,7 @@ struct PermuteParams {
   const int* T_dev;    // as RouteParams::T_dev
   float* zero_rows;    // when set, rows t of this [T, H] fp32 buffer are zeroed for every token
   int* assign_row;     // when set, [T, top_k]: permuted row of every assignment, -1 if not local
+  int n_shared;        // 1: token t also fills row 128 * tile_start[E_local] + t, weight 1
 };
 
 // One persistent grouped GEMM launch.  Work units are (expert tile, N tile)
@@ -76,7 +81,7 @@ struct PermuteParams {
 struct GemmParams {
   const int* tile_start;   // [E_local + 1] prefix sum of 128-row tiles
   const int* counts;       // [E_local] rows per expert
-  int E_local;
+  int E_local;             // dispatch buckets: local experts (+ the shared expert), <= kMaxBuckets
   int num_k_blocks;        // K / 128
   int n_tiles;             // N tiles of 256 output columns
   int b_rows_per_expert;   // rows of one expert's weight matrix (2I or H)
@@ -129,7 +134,7 @@ struct GuardList {
 };
 
 struct CheckParams {
-  int T, top_k, E_global, E_local, local_expert_offset;
+  int T, top_k, E_global, E_local, local_expert_offset, n_shared;
   int64_t npad;
   const int* counts;
   const int* tile_start;
@@ -155,10 +160,12 @@ __global__ void moe_route_permute_tiny_kernel(RouteParams rp, PermuteParams pp, 
 __global__ void moe_finalize_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out,
                                     int64_t n8);
 // Deterministic combine: out[t] = bf16(sum over k of rows_out[assign_row[t, k]]),
-// k in routing-selection order.
+// k in routing-selection order, then the shared expert's row 128 * *shared_tile
+// + t when shared_tile is set.
 __global__ void moe_combine_rows_kernel(const float* __restrict__ rows_out,
                                         const int* __restrict__ assign_row,
-                                        __nv_bfloat16* __restrict__ out, int T, int H, int top_k);
+                                        __nv_bfloat16* __restrict__ out, int T, int H, int top_k,
+                                        const int* __restrict__ shared_tile);
 
 constexpr int kGemm1 = 0;   // gate/up GEMM, SwiGLU + 1x64 FP8 requant epilogue
 constexpr int kGemm2 = 1;   // down GEMM, routing-weighted scatter-add epilogue

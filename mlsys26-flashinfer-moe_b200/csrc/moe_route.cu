@@ -271,7 +271,14 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(RouteParams p)
   for (int w = 0; w < warp; ++w) before += warp_sum[w];
   incl += before;
   if (tid < p.E_local) p.tile_start[tid] = incl - tiles;
-  if (tid == kRouteThreads - 1) p.tile_start[p.E_local] = incl;
+  if (tid == kRouteThreads - 1) {
+    p.tile_start[p.E_local] = incl;
+    if (p.n_shared) {   // the shared expert's bucket: every token, in order
+      const int T = p.T_dev ? min(p.T, *p.T_dev) : p.T;
+      p.counts[p.E_local] = T;
+      p.tile_start[p.E_local + 1] = incl + (T + kTileM - 1) / kTileM;
+    }
+  }
   if (tid == 0) p.ctrl->done = 0u;
 }
 
@@ -383,7 +390,8 @@ __device__ __forceinline__ void pack_rows(const PermuteParams& p, const int* row
 // Exclusive scan of the experts' 128-row tile counts (one thread per local
 // expert, E_local <= kRouteThreads): writes tile_start[0..E_local] and returns
 // this thread's start.
-__device__ __forceinline__ int scan_tiles(int tiles, int* tile_start, int E_local, int* warp_sum) {
+__device__ __forceinline__ int scan_tiles(int tiles, int* tile_start, int E_local, int* warp_sum,
+                                          int shared_rows) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int incl = tiles;
 #pragma unroll
@@ -397,8 +405,51 @@ __device__ __forceinline__ int scan_tiles(int tiles, int* tile_start, int E_loca
   for (int w = 0; w < warp; ++w) before += warp_sum[w];
   incl += before;
   if (tid < E_local) tile_start[tid] = incl - tiles;
-  if (tid == kRouteThreads - 1) tile_start[E_local] = incl;
+  if (tid == kRouteThreads - 1) {
+    tile_start[E_local] = incl;
+    if (shared_rows >= 0) tile_start[E_local + 1] = incl + (shared_rows + kTileM - 1) / kTileM;
+  }
   return incl - tiles;
+}
+
+// Shared expert: token t of [t0, t1) fills row base + t with weight 1 (its
+// token id, scales and FP8 row), shared out over `nsub` blocks as pack_rows.
+__device__ __forceinline__ void pack_shared_rows(const PermuteParams& p, int64_t base, int t0, int t1,
+                                                 int sub, int nsub) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = t1 - t0;
+  const int nthreads = blockDim.x * nsub, first = sub * blockDim.x + tid;
+  for (int j = first; j < n; j += nthreads) {
+    p.row_token[base + t0 + j] = t0 + j;
+    p.row_weight[base + t0 + j] = 1.f;
+  }
+  // scales [H/128, *]: consecutive threads take consecutive tokens of one block
+  const int hb = p.H / kBlockK;
+  const int64_t n_sc = static_cast<int64_t>(n) * hb;
+  for (int64_t i = first; i < n_sc; i += nthreads) {
+    const int kb = static_cast<int>(i / n), j = static_cast<int>(i - static_cast<int64_t>(kb) * n);
+    p.a_scale_perm[static_cast<int64_t>(kb) * p.npad + base + t0 + j] =
+        __ldg(p.hs_scale + static_cast<int64_t>(kb) * p.scale_ld + t0 + j);
+  }
+  const int vec = p.H / 16;
+  const int nwarps = blockDim.x >> 5;
+  for (int j = sub * nwarps + warp; j < n; j += nwarps * nsub) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(t0 + j) * p.H);
+    uint4* dst = reinterpret_cast<uint4*>(p.a_perm + (base + t0 + j) * p.H);
+    for (int c0 = 0; c0 < vec; c0 += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + 32 * i + lane;
+        if (c < vec) v[i] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + 32 * i + lane;
+        if (c < vec) dst[c] = v[i];
+      }
+    }
+  }
 }
 
 }  // namespace
@@ -422,6 +473,9 @@ __global__ void __launch_bounds__(kRouteThreads) moe_permute_kernel(PermuteParam
   if (warp == 0) assign_rows(p, p.topk_idx, cursor, rows_s, t0, t1, lane);
   __syncthreads();
   pack_rows(p, rows_s, t0, t1, blockIdx.y, gridDim.y);
+  if (p.n_shared)
+    pack_shared_rows(p, static_cast<int64_t>(kTileM) * p.tile_start[p.E_local], t0, t1, blockIdx.y,
+                     gridDim.y);
 }
 
 // Decode-sized batches (T <= kTinyMaxTokens, host row count): routing, the
@@ -463,13 +517,16 @@ __global__ void __launch_bounds__(kRouteThreads)
   __syncthreads();
   const int count = tid < rp.E_local ? hist_s[tid] : 0;
   if (tid < rp.E_local) rp.counts[tid] = count;
+  if (tid == 0 && rp.n_shared) rp.counts[rp.E_local] = rp.T;
   const int first = scan_tiles(tid < rp.E_local ? (count + kTileM - 1) / kTileM : 0, rp.tile_start,
-                               rp.E_local, warp_sum);
+                               rp.E_local, warp_sum, rp.n_shared ? rp.T : -1);
   if (tid < rp.E_local) cursor[tid] = kTileM * first;
-  __syncthreads();
+  __syncthreads();   // also publishes tile_start[E_local] (written above) to the block
   if (warp == 0) assign_rows(pp, idx_s, cursor, rows_s, 0, rp.T, lane);
   __syncthreads();
   pack_rows(pp, rows_s, 0, rp.T, 0, 1);
+  if (pp.n_shared)
+    pack_shared_rows(pp, static_cast<int64_t>(kTileM) * rp.tile_start[rp.E_local], 0, rp.T, 0, 1);
 }
 
 __global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restrict__ in,
@@ -492,8 +549,10 @@ __global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restri
 
 __global__ void __launch_bounds__(256)
     moe_combine_rows_kernel(const float* __restrict__ rows_out, const int* __restrict__ assign_row,
-                            __nv_bfloat16* __restrict__ out, int T, int H, int top_k) {
+                            __nv_bfloat16* __restrict__ out, int T, int H, int top_k,
+                            const int* __restrict__ shared_tile) {
   griddep_wait();   // GEMM2's rows are complete
+  const int64_t shared_base = shared_tile ? static_cast<int64_t>(kTileM) * *shared_tile : -1;
   const int n8 = H / 8;
   const int64_t total = static_cast<int64_t>(T) * n8;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -506,6 +565,12 @@ __global__ void __launch_bounds__(256)
       const int r = __ldg(assign_row + static_cast<int64_t>(t) * top_k + k);
       if (r < 0) continue;
       const float4* src = reinterpret_cast<const float4*>(rows_out + static_cast<int64_t>(r) * H) + 2 * c8;
+      const float4 a = __ldcs(src), b = __ldcs(src + 1);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    if (shared_base >= 0) {   // the shared expert's row, last
+      const float4* src = reinterpret_cast<const float4*>(rows_out + (shared_base + t) * H) + 2 * c8;
       const float4 a = __ldcs(src), b = __ldcs(src + 1);
       acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
       acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;

@@ -67,6 +67,7 @@ class MoeFwdArgs(ctypes.Structure):
         ("reserved", ctypes.c_uint32),
         ("wait_limit_ns", ctypes.c_uint64),
         ("gemm2_weights_bf16", ctypes.c_void_p),
+        ("n_shared_experts", ctypes.c_int64),
     ]
 
 

@@ -61,7 +61,7 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                local_expert_offset: int, routed_scaling_factor: float, output: torch.Tensor,
                n_group: int = 8, topk_group: int = 4, top_k: int = 8,
                deterministic: bool = False, gemm2_weights_bf16: Optional[torch.Tensor] = None,
-               debug: bool = False):
+               debug: bool = False, n_shared_experts: int = 0):
     """Validate like the reference and fill a ``MoeFwdArgs`` (no workspace yet).
 
     ``deterministic`` selects the fixed-order combine (``MOE_FLAG_DETERMINISTIC``):
@@ -70,7 +70,9 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     same down-projection weights prepared by ``prepare_gemm2_weights`` (bf16
     GEMM2 without block-scale promotion on the prefill path).  ``debug`` sets
     ``MOE_FLAG_DEBUG`` (device checks of the dispatch tables and workspace
-    guards).
+    guards).  ``n_shared_experts=1``: the weight tensors hold the local routed
+    experts followed by DeepSeek-V3's shared expert (``[E_local + 1, ...]``),
+    which every token also goes through with weight 1.
 
     Returns ``(args, keepalive, out_dev)``: ``keepalive`` holds the device
     copies the pointers refer to; ``out_dev`` is where the kernel writes (the
@@ -87,17 +89,20 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     assert routing_logits.dim() == 2, "routing_logits must be [T, E_global]"
     t, e_global = int(routing_logits.shape[0]), int(routing_logits.shape[1])
     assert gemm1_weights.dim() == 3, "gemm1_weights must be [E_local, 2I, H]"
-    e_local, i2, h = (int(x) for x in gemm1_weights.shape)
+    assert n_shared_experts in (0, 1), "n_shared_experts must be 0 or 1"
+    e_all, i2, h = (int(x) for x in gemm1_weights.shape)
+    e_local = e_all - int(n_shared_experts)   # routed experts; the shared one follows them
+    assert e_local >= 1, "gemm1_weights must hold at least one routed expert"
     i = i2 // 2
     assert i2 == 2 * i, "gemm1_weights second dim must be 2*I"
     assert routing_bias.numel() == e_global, f"routing_bias must have {e_global} entries"
     assert hidden_states.shape == (t, h), f"hidden_states must be [{t}, {h}]"
     assert hidden_states_scale.shape == (h // 128, t), f"hidden_states_scale must be [{h // 128}, {t}]"
-    assert gemm1_weights_scale.shape == (e_local, i2 // 128, h // 128), \
-        f"gemm1_weights_scale must be [{e_local}, {i2 // 128}, {h // 128}]"
-    assert gemm2_weights.shape == (e_local, h, i), f"gemm2_weights must be [{e_local}, {h}, {i}]"
-    assert gemm2_weights_scale.shape == (e_local, h // 128, i // 128), \
-        f"gemm2_weights_scale must be [{e_local}, {h // 128}, {i // 128}]"
+    assert gemm1_weights_scale.shape == (e_all, i2 // 128, h // 128), \
+        f"gemm1_weights_scale must be [{e_all}, {i2 // 128}, {h // 128}]"
+    assert gemm2_weights.shape == (e_all, h, i), f"gemm2_weights must be [{e_all}, {h}, {i}]"
+    assert gemm2_weights_scale.shape == (e_all, h // 128, i // 128), \
+        f"gemm2_weights_scale must be [{e_all}, {h // 128}, {i // 128}]"
     assert output.shape == (t, h), f"output must be [{t}, {h}]"
     assert 0 <= int(local_expert_offset) and int(local_expert_offset) + e_local <= e_global, \
         "local experts must lie inside [0, E_global)"
@@ -125,6 +130,7 @@ def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     a.bias_dtype = _BIAS_DTYPES[routing_bias.dtype]
     a.flags = (_lib.MOE_FLAG_DETERMINISTIC if deterministic else 0) | \
         (_lib.MOE_FLAG_DEBUG if debug else 0)
+    a.n_shared_experts = int(n_shared_experts)
     if gemm2_weights_bf16 is not None:
         assert gemm2_weights_bf16.dtype == torch.bfloat16 and \
             gemm2_weights_bf16.shape == (e_local, h, i), \
@@ -181,7 +187,8 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
         routed_scaling_factor: float, output: torch.Tensor, *, n_group: int = 8,
         topk_group: int = 4, top_k: int = 8, workspace: Optional[torch.Tensor] = None,
         deterministic: bool = False,
-        gemm2_weights_bf16: Optional[torch.Tensor] = None, debug: bool = False) -> None:
+        gemm2_weights_bf16: Optional[torch.Tensor] = None, debug: bool = False,
+        n_shared_experts: int = 0) -> None:
     """Fused FP8 block-scale DeepSeek-V3 MoE forward (reference ``kernel.py:562``).
 
     Writes the bf16 ``[T, H]`` layer output into ``output``.  Only the experts
@@ -196,12 +203,16 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     checks the routing and dispatch tables on the device before the GEMMs use
     them and guards every workspace buffer; it then waits for the forward and
     raises ``MoeError`` (a ``RuntimeError``) naming the failed check.
+    ``n_shared_experts=1`` adds DeepSeek-V3's shared expert, passed as the last
+    slice of each weight tensor (``[E_local + 1, ...]``), with weight 1; the
+    reference computes the routed sum only.
     """
     args, keep, out_dev = build_args(routing_logits, routing_bias, hidden_states,
                                      hidden_states_scale, gemm1_weights, gemm1_weights_scale,
                                      gemm2_weights, gemm2_weights_scale, local_expert_offset,
                                      routed_scaling_factor, output, n_group, topk_group, top_k,
-                                     deterministic, gemm2_weights_bf16, debug)
+                                     deterministic, gemm2_weights_bf16, debug,
+                                     n_shared_experts)
     device = keep[0].device
     if args.T > 0:
         forward_args(args, workspace, device)
@@ -352,6 +363,7 @@ def workspace_views(args: _lib.MoeFwdArgs, workspace: torch.Tensor) -> dict:
     """Typed views of the per-stage buffers a forward leaves in ``workspace``."""
     lay = workspace_layout(args)
     t, k, el, h, i = args.T, args.top_k, args.E_local, args.H, args.I
+    nb = el + args.n_shared_experts   # dispatch buckets
     npad = lay.npad
 
     def view(off, n, dtype):
@@ -362,8 +374,8 @@ def workspace_views(args: _lib.MoeFwdArgs, workspace: torch.Tensor) -> dict:
         layout=lay,
         topk_idx=view(lay.topk_idx, t * k, torch.int32).view(t, k),
         topk_weights=view(lay.topk_weights, t * k, torch.float32).view(t, k),
-        counts=view(lay.counts, el, torch.int32),
-        tile_start=view(lay.tile_start, el + 1, torch.int32),
+        counts=view(lay.counts, nb, torch.int32),
+        tile_start=view(lay.tile_start, nb + 1, torch.int32),
         row_token=view(lay.row_token, npad, torch.int32),
         row_weight=view(lay.row_weight, npad, torch.float32),
         a_perm=view(lay.a_perm, npad * h, torch.uint8).view(npad, h),

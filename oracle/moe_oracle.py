@@ -265,7 +265,7 @@ def expert_forward(a_codes, a_scale_t, w1q, w1s, w2q, w2s, inter: int, requant: 
 
 def moe_forward(inp: dict, n_group: int, topk_group: int, top_k: int, requant: bool = True,
                 block: int = 64, tokens: np.ndarray | None = None, return_parts: bool = False,
-                get_expert=None):
+                get_expert=None, n_shared: int = 0):
     """Whole layer, as ``run()`` computes it (kernel.py:562-729).
 
     ``inp`` holds numpy arrays: ``routing_logits [T,E]``, ``routing_bias [E]``,
@@ -277,6 +277,12 @@ def moe_forward(inp: dict, n_group: int, topk_group: int, top_k: int, requant: b
     checks cheap.  ``get_expert(e)`` may supply ``(w1q, w1s, w2q, w2s)`` of
     local expert ``e`` lazily instead of the four weight arrays in ``inp``.  Returns the fp32 ``[T or len(tokens), H]`` sum before the
     bf16 cast; ``bf16_bits`` of it is the reference's ``output``.
+
+    ``n_shared=1`` adds DeepSeek-V3's shared expert, which the reference does
+    not have: the weight arrays then hold the routed experts followed by the
+    shared one (index ``e_local``), and every token's output gains that
+    expert's output with weight 1 after its routed sum (y = sum_k w_k E_k(x) +
+    S(x)), computed by the same ``expert_forward`` (1x64 requant included).
     """
     logits = inp["routing_logits"]
     t = logits.shape[0]
@@ -286,7 +292,7 @@ def moe_forward(inp: dict, n_group: int, topk_group: int, top_k: int, requant: b
         def get_expert(e):
             return (inp["gemm1_weights"][e], inp["gemm1_weights_scale"][e],
                     inp["gemm2_weights"][e], inp["gemm2_weights_scale"][e])
-        e_local = inp["gemm1_weights"].shape[0]
+        e_local = inp["gemm1_weights"].shape[0] - n_shared
     else:
         e_local = int(inp["e_local"])
     h = inp["hidden_states"].shape[1]
@@ -313,6 +319,11 @@ def moe_forward(inp: dict, n_group: int, topk_group: int, top_k: int, requant: b
         # weighted scatter-add (kernel.py:236-250), fp32
         for r, tok in enumerate(rows_tok):
             out[pos[int(tok)]] += (y[r] * rows_w[r]).astype(np.float32)
+    if n_shared:
+        w1q, w1s, w2q, w2s = get_expert(e_local)
+        y = expert_forward(hs[sel], hss[:, sel], w1q, w1s, w2q, w2s, w1q.shape[0] // 2, requant,
+                           block)
+        out += y.astype(np.float32)
     if return_parts:
         return out, dict(idx=idx, w=w, counts=counts, starts=starts, tokens=btok, weights=bw,
                          parts=parts)

@@ -62,10 +62,10 @@ def host_inputs(inp: dict, shape) -> dict:
     return out
 
 
-def oracle_output(inp: dict, shape, tokens=None, requant=True):
+def oracle_output(inp: dict, shape, tokens=None, requant=True, n_shared=0):
     hi = host_inputs(inp, shape)
     return mo.moe_forward(hi, shape.n_group, shape.topk_group, shape.top_k, requant=requant,
-                          tokens=tokens, get_expert=lazy_expert_getter(inp))
+                          tokens=tokens, get_expert=lazy_expert_getter(inp), n_shared=n_shared)
 
 
 def check_routing_and_dispatch(views, inp, shape):
