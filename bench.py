@@ -78,6 +78,9 @@ def parse():
                     help="router bias +10 on the local experts, so every token's experts are "
                          "local: T=1 with --e-local 8 does the work of a 256-expert decode step "
                          "with 0.35 GB of weights resident (for ncu captures)")
+    ap.add_argument("--router-bias", action="store_true",
+                    help="headline with config 1's router bias N(0, 0.1) instead of config 2's "
+                         "uniform routing (zero bias)")
     ap.add_argument("--prepared-w2", action="store_true",
                     help="headline run with the one-time bf16 relayout of W2 (bf16 GEMM2)")
     ap.add_argument("--flashinfer-contest", action="store_true", help=argparse.SUPPRESS)
@@ -212,7 +215,7 @@ def layer_inputs(weights, shape, seed, zipf=None, zero_bias=False):
 class Runner:
     """Holds inputs, workspace and events for repeated forwards of one shape."""
 
-    def __init__(self, torch, shape, inp, gemm2_weights_bf16=None):
+    def __init__(self, torch, shape, inp, gemm2_weights_bf16=None, n_shared=0):
         from moe_b200 import api, _lib
         self.torch, self.api, self._lib, self.shape = torch, api, _lib, shape
         self.inp = inp
@@ -220,7 +223,8 @@ class Runner:
         from moe_b200 import workloads
         self.args, self.keep, _ = api.build_args(*workloads.run_args(self.inp), self.out,
                                                  shape.n_group, shape.topk_group, shape.top_k,
-                                                 gemm2_weights_bf16=gemm2_weights_bf16)
+                                                 gemm2_weights_bf16=gemm2_weights_bf16,
+                                                 n_shared_experts=n_shared)
         lay = api.workspace_layout(self.args)
         self.ws = torch.empty(lay.total_bytes, dtype=torch.uint8, device="cuda")
         self.args.workspace = self.ws.data_ptr()
@@ -368,6 +372,8 @@ def run_ours(a):
     shape = workloads.dsv3_shape(t, e_local=a.e_local)
     if a.zipf is None:
         inp = {k: (v[:shape.e_local] if k in WEIGHT_KEYS else v) for k, v in weights.items()}
+        if not a.router_bias:   # config 2: uniform random routing, logits N(0,1) and no bias
+            inp["routing_bias"] = torch.zeros_like(weights["routing_bias"])
     else:
         inp = layer_inputs(weights, shape, seed=0, zipf=a.zipf)
     if a.concentrate:
@@ -418,6 +424,9 @@ def run_ours(a):
     }
     cfg_name = "config 3, Zipf routing" if a.zipf is not None else \
         ("config 2" if shape.e_local == 256 else "same-density subset")
+    if a.zipf is None:
+        cfg_name += (", router bias N(0, 0.1)" if a.router_bias
+                     else ", uniform random routing (zero router bias)")
     if a.concentrate:
         cfg_name = "routing concentrated on the local experts, profiling case"
     if a.prepared_w2:
@@ -452,11 +461,14 @@ def run_ours(a):
         torch.cuda.empty_cache()
         line["prepared_gemm2_bf16"] = prepared_run(torch, shape, inp, fp8_peak, a)
         line["prefill_sweep"] = prefill_sweep(torch, weights, fp8_peak, a)
+        line["router_bias_t8192"] = biased_run(torch, weights, fp8_peak, a)
         line["zipf_t8192"] = zipf_run(torch, weights, fp8_peak, a)
         line["ep_config_n1"] = ep_config_n1(torch, weights, a)
         line["decode"] = decode_sweep(torch, weights, peaks)
         line["contest_shape"] = contest_sweep(torch, weights)
-        tps, dt, ns, threads = cpu_baseline(full, weights, a.cpu_sample_tokens, torch)
+        line["neighbours"] = neighbours(torch, weights, fp8_peak, peaks, line["decode"])
+        tps, dt, ns, threads = cpu_baseline(full, {**weights, "routing_bias": inp["routing_bias"]},
+                                            a.cpu_sample_tokens, torch)
         line["cpu_baseline"] = {"value": round(tps, 3), "unit": "tokens/s", "cores": threads,
                                 "kind": "port",
                                 "sample": f"first {ns} tokens of the T={t} batch through the numpy "
@@ -557,15 +569,32 @@ def prepared_run(torch, shape, inp, fp8_peak, a):
 
 
 def prefill_sweep(torch, weights, fp8_peak, a):
-    """Config 2 at the other token counts (all 256 experts, uniform routing)."""
+    """Config 2 at the other token counts (all 256 experts, uniform routing:
+    logits N(0,1), zero router bias)."""
     from moe_b200 import workloads
     res = {}
     for t in (1024, 4096, 16384):
         shape = workloads.dsv3_shape(t)
-        r = Runner(torch, shape, layer_inputs(weights, shape, seed=30 + t))
+        r = Runner(torch, shape, layer_inputs(weights, shape, seed=30 + t, zero_bias=True))
         res[str(t)] = prefill_point(torch, r, 10, 3, fp8_peak)
         del r
         torch.cuda.empty_cache()
+    return res
+
+
+def biased_run(torch, weights, fp8_peak, a):
+    """The headline size with config 1's router bias N(0, 0.1) instead of
+    uniform routing (the headline workload of earlier measurements): the bias
+    leaves ~36 experts idle and gives the hottest ~8x the mean rows."""
+    from moe_b200 import workloads
+    shape = workloads.dsv3_shape(8192)
+    inp = {k: (v[:256] if k in WEIGHT_KEYS else v) for k, v in weights.items()}
+    r = Runner(torch, shape, inp)
+    res = prefill_point(torch, r, 10, 3, fp8_peak)
+    counts = r.views()["counts"].float()
+    res["max_rows"] = int(counts.max().item())
+    del r
+    torch.cuda.empty_cache()
     return res
 
 
@@ -666,6 +695,95 @@ def decode_sweep(torch, weights, peaks):
                        "stage_us": {k: round(v * 1e3, 1) for k, v in stages.items()}}
         del graph, r
         torch.cuda.empty_cache()
+    return res
+
+
+def with_shared_expert(torch, inp, shape, seed):
+    """``inp`` with one more expert after the local ones (the workloads' weight
+    recipe): DeepSeek-V3's shared expert in the layout n_shared_experts=1 takes."""
+    from moe_b200 import workloads
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    h, i = shape.hidden, shape.inter
+    w1 = (0.02 * torch.randn(1, 2 * i, h, generator=g, device="cuda")).to(torch.bfloat16)
+    w2 = (0.02 * torch.randn(1, h, i, generator=g, device="cuda")).to(torch.bfloat16)
+    (q1, s1), (q2, s2) = workloads.quantize_weight_blocks(w1), workloads.quantize_weight_blocks(w2)
+    out = dict(inp)
+    for k, v in (("gemm1_weights", q1), ("gemm1_weights_scale", s1), ("gemm2_weights", q2),
+                 ("gemm2_weights_scale", s2)):
+        out[k] = torch.cat([inp[k], v])
+    return out
+
+
+def neighbours(torch, weights, fp8_peak, peaks, decode):
+    """The ops either side of run(): the router GEMM that produces
+    routing_logits, and DeepSeek-V3's shared expert fused into the layer as one
+    more dispatch bucket (n_shared_experts=1, all 256 routed experts local)."""
+    from moe_b200 import workloads, LayerGraph, router_logits
+    res = {}
+    h, e = 7168, 256
+    rl = {}
+    for t in (1, 64, 8192):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(5000 + t)
+        x = torch.randn(t, h, generator=g, device="cuda").to(torch.bfloat16)
+        w = (0.02 * torch.randn(e, h, generator=g, device="cuda")).to(torch.bfloat16)
+        out = torch.empty(t, e, device="cuda")
+        for _ in range(3):
+            router_logits(x, w, out)
+        torch.cuda.synchronize()
+        n = 20
+        s, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            router_logits(x, w, out)
+        en.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(en) / n * 1e3
+        byts = 2 * t * h + 2 * e * h + 4 * t * e
+        rl[str(t)] = {"us": round(us, 1), "tflops": round(2 * t * h * e / (us * 1e-6) / 1e12, 2),
+                      "gbs": round(byts / (us * 1e-6) / 1e9, 1),
+                      "hbm_roofline_us": round(byts / (peaks["hbm_gbs"] * 1e9) * 1e6, 2),
+                      "path": "CUDA cores, fixed order" if t <= 128 else "tcgen05 kind::f16"}
+    res["router_logits"] = {"shape": f"x [T, {h}] bf16 . w_gate [{e}, {h}]^T -> fp32",
+                            "timing": "mean of 20 back-to-back calls (w_gate 3.7 MB stays in L2)",
+                            "by_tokens": rl}
+    # shared expert at the headline size
+    shape = workloads.dsv3_shape(8192)
+    inp = with_shared_expert(torch, layer_inputs(weights, shape, seed=0, zero_bias=True), shape,
+                             seed=77)
+    r = Runner(torch, shape, inp, n_shared=1)
+    pt = prefill_point(torch, r, 10, 3, fp8_peak)
+    pt["note"] = ("the headline's tokens and routing plus the shared expert: 257 dispatch "
+                  "buckets; flops count the shared expert's T rows with the 8T routed ones")
+    res["shared_expert_t8192"] = pt
+    del r, inp
+    torch.cuda.empty_cache()
+    # shared expert at decode sizes: graph replay p50, L2 flushed
+    flush_buf = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    dec = {}
+    for t in (1, 8):
+        shape = workloads.dsv3_shape(t)
+        inp = with_shared_expert(torch, layer_inputs(weights, shape, seed=1), shape, seed=78)
+        out_g = torch.empty(t, shape.hidden, dtype=torch.bfloat16, device="cuda")
+        graph = LayerGraph(*workloads.run_args(inp), out_g, n_shared_experts=1)
+        per = []
+        for i in range(35):
+            flush_buf.zero_()
+            s, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            graph.replay()
+            en.record()
+            en.synchronize()
+            if i >= 5:
+                per.append(s.elapsed_time(en))
+        dec[str(t)] = {"p50_us_graph": round(statistics.median(per) * 1e3, 1),
+                       "routed_only_p50_us_graph": decode.get(str(t), {}).get("p50_us_graph")}
+        del graph, inp
+        torch.cuda.empty_cache()
+    res["shared_expert_decode"] = dec
+    del flush_buf
+    torch.cuda.empty_cache()
     return res
 
 
@@ -1041,6 +1159,7 @@ def run_reference(a):
     # GPU when there is one (fast) and copied per expert
     sshape = workloads.dsv3_shape(sample)
     inp = workloads.make_inputs(sshape, seed=0, device=dev)
+    inp["routing_bias"] = torch.zeros_like(inp["routing_bias"])   # config 2: uniform routing
     times = []
     threads = os.cpu_count() or 1
     for i in range(a.warmup + a.steps):

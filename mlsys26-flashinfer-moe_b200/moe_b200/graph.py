@@ -26,7 +26,8 @@ class LayerGraph:
     dtypes on one device (no implicit copies are allowed, since a copy made at
     capture time would never see later updates).  They stay borrowed for the
     graph's lifetime.  ``replay()`` runs on ``stream`` (default: the current
-    stream at replay time) and writes ``output``.
+    stream at replay time) and writes ``output``.  ``deterministic`` and
+    ``n_shared_experts`` are those of ``run()``.
     """
 
     def __init__(self, routing_logits: torch.Tensor, routing_bias: torch.Tensor,
@@ -34,14 +35,16 @@ class LayerGraph:
                  gemm1_weights: torch.Tensor, gemm1_weights_scale: torch.Tensor,
                  gemm2_weights: torch.Tensor, gemm2_weights_scale: torch.Tensor,
                  local_expert_offset: int, routed_scaling_factor: float, output: torch.Tensor,
-                 *, n_group: int = 8, topk_group: int = 4, top_k: int = 8):
+                 *, n_group: int = 8, topk_group: int = 4, top_k: int = 8,
+                 deterministic: bool = False, n_shared_experts: int = 0):
         given = dict(routing_logits=routing_logits, routing_bias=routing_bias,
                      hidden_states=hidden_states, hidden_states_scale=hidden_states_scale,
                      gemm1_weights=gemm1_weights, gemm1_weights_scale=gemm1_weights_scale,
                      gemm2_weights=gemm2_weights, gemm2_weights_scale=gemm2_weights_scale)
         args, keep, out_dev = api.build_args(*given.values(), local_expert_offset,
                                              routed_scaling_factor, output, n_group, topk_group,
-                                             top_k)
+                                             top_k, deterministic=deterministic,
+                                             n_shared_experts=n_shared_experts)
         for (name, t), k in zip(given.items(), keep):
             if k.data_ptr() != t.data_ptr():
                 raise ValueError(f"{name} must be a contiguous tensor on the output's CUDA device")
