@@ -75,10 +75,10 @@ bool use_small_path(const MoeFwdArgs* a) {
          a->H / kBlockK <= kSmallMaxScaleBlocks && a->I / 64 <= kSmallMaxScaleBlocks;
 }
 
-Layout make_layout(const MoeFwdArgs* a) {
+Layout make_layout(const MoeFwdArgs* a, int target_blocks = kRouteTargetBlocks) {
   Layout L{};
   const int64_t T = a->T, H = a->H, I = a->I, El = a->E_local, K = a->top_k;
-  int64_t tpw = (T + kRouteTargetBlocks * 8 - 1) / (kRouteTargetBlocks * 8);
+  int64_t tpw = (T + target_blocks * 8 - 1) / (target_blocks * 8);
   if (tpw < 1) tpw = 1;
   int64_t tpb = 8 * tpw;
   if (tpb > kMaxTokensPerBlock) tpb = kMaxTokensPerBlock;
@@ -863,7 +863,7 @@ extern "C" int moe_fp8_route_noalloc(const float* routing_logits, const void* ro
   if (T == 0) return MOE_OK;
   if (!routing_logits || !routing_bias || !topk_idx || !topk_weights || !expert_counts)
     return MOE_ERR_INVALID_ARG;
-  const Layout L = make_layout(&a);
+  const Layout L = make_layout(&a, kNoAllocMaxBlocks);
   if (L.blocks > kNoAllocMaxBlocks) return MOE_ERR_TOO_LARGE;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev))) return st;
