@@ -319,17 +319,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float* ws = p.b_scale + static_cast<int64_t>(c.e) * (2 * ib_rows) * KB;
         const float* ws_x1 = ws + static_cast<int64_t>(c.n) * KB;
         const float* ws_x2 = ws + static_cast<int64_t>(ib_rows + c.n) * KB;
-        // Scales of K block kb+1 are loaded while block kb is promoted.
-        float sa_n = warp_active ? __ldg(p.a_scale + grow) : 0.f;
+        // Scales of K block kb+2 are loaded while block kb is promoted: the
+        // permuted activation scales come from DRAM (the permute's row copies
+        // push them out of L2), and a load issued one K block ahead still
+        // stalled every group's first multiply (clock64 traces: ~300 of ~1000
+        // cycles per group).
+        const float* sa_p = p.a_scale + grow;
+        float sa_n = warp_active ? __ldg(sa_p) : 0.f;
         float w1_n = __ldg(ws_x1), w2_n = __ldg(ws_x2);
+        float sa_nn = 0.f, w1_nn = 0.f, w2_nn = 0.f;
+        if (KB > 1) {
+          if (warp_active) sa_nn = __ldg(sa_p + p.npad);
+          w1_nn = __ldg(ws_x1 + 1);
+          w2_nn = __ldg(ws_x2 + 1);
+        }
         for (int kb = 0; kb < KB; ++kb) {
           const float s1 = sa_n * w1_n;
           const float s2 = sa_n * w2_n;
-          if (kb + 1 < KB) {
-            if (warp_active)
-              sa_n = __ldg(p.a_scale + static_cast<int64_t>(kb + 1) * p.npad + grow);
-            w1_n = __ldg(ws_x1 + kb + 1);
-            w2_n = __ldg(ws_x2 + kb + 1);
+          sa_n = sa_nn;
+          w1_n = w1_nn;
+          w2_n = w2_nn;
+          if (kb + 2 < KB) {
+            if (warp_active) sa_nn = __ldg(sa_p + static_cast<int64_t>(kb + 2) * p.npad);
+            w1_nn = __ldg(ws_x1 + kb + 2);
+            w2_nn = __ldg(ws_x2 + kb + 2);
           }
           const uint32_t buf = g & 1u;
           if (!next_ready && !mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 4))
@@ -358,14 +371,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ++g;
         }
         // SwiGLU + 1x64 requant (kernel.py:128-151).  The MMA is stalled while
-        // this runs, so it uses one reciprocal per element for the sigmoid and
-        // one IEEE reciprocal of the scale per row instead of 128 divisions.
+        // this runs (two groups ahead at most), so silu(x) = x / (1 + exp(-x))
+        // uses the fast division (reciprocal approximation and multiply, within
+        // 2 ulp of the IEEE quotient; the accumulators themselves differ from
+        // the reference's in summation order by far more) and the requant one
+        // IEEE reciprocal of the scale per row instead of 64 divisions.  The
+        // IEEE-rounded reciprocal per element cost 8-9% of GEMM1 at T=8192-16384.
         if (warp_active) {
           float amax = 0.f;
 #pragma unroll
           for (int j = 0; j < 64; ++j) {
             const float x1 = acc[j], x2 = acc[64 + j];
-            const float cval = (x2 * __frcp_rn(1.0f + __expf(-x2))) * x1;
+            const float cval = __fdividef(x2, 1.0f + __expf(-x2)) * x1;
             acc[j] = cval;
             amax = fmaxf(amax, fabsf(cval));
           }
@@ -458,21 +475,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         } else {
         // W2 scale [E, H/128, I/128]: row block 2n + h of this thread's columns.
         const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * kb_rows + 2 * c.n + h) * KB;
-        // Both intermediate scales of K block kb+1 and its weight scale are
-        // loaded at the top of K block kb, a full K block (two groups) ahead
-        // of their use.
+        // Both intermediate scales of K block kb+2 and its weight scale are
+        // loaded at the top of K block kb, two K blocks (four groups) ahead of
+        // their use, as in GEMM1.
         const float* sa_p = p.a_scale + grow;
         float sa0_n = warp_active ? __ldg(sa_p) : 0.f;
         float sa1_n = warp_active ? __ldg(sa_p + p.npad) : 0.f;
         float sw_n = __ldg(ws);
+        float sa0_nn = 0.f, sa1_nn = 0.f, sw_nn = 0.f;
+        if (KB > 1) {
+          if (warp_active) {
+            sa0_nn = __ldg(sa_p + 2 * p.npad);
+            sa1_nn = __ldg(sa_p + 3 * p.npad);
+          }
+          sw_nn = __ldg(ws + 1);
+        }
         for (int kb = 0; kb < KB; ++kb) {
           const float sg0 = sa0_n * sw_n, sg1 = sa1_n * sw_n;
-          if (kb + 1 < KB) {
+          sa0_n = sa0_nn;
+          sa1_n = sa1_nn;
+          sw_n = sw_nn;
+          if (kb + 2 < KB) {
             if (warp_active) {
-              sa0_n = __ldg(sa_p + static_cast<int64_t>(2 * kb + 2) * p.npad);
-              sa1_n = __ldg(sa_p + static_cast<int64_t>(2 * kb + 3) * p.npad);
+              sa0_nn = __ldg(sa_p + static_cast<int64_t>(2 * kb + 4) * p.npad);
+              sa1_nn = __ldg(sa_p + static_cast<int64_t>(2 * kb + 5) * p.npad);
             }
-            sw_n = __ldg(ws + kb + 1);
+            sw_nn = __ldg(ws + kb + 2);
           }
 #pragma unroll
           for (int gi = 0; gi < 2; ++gi) {

@@ -500,7 +500,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
 #pragma unroll
         for (int j = 0; j < kSmallN; ++j) {
           const float x1 = acc[j], x2 = acc[kSmallN + j];
-          cv[j] = (x2 * __frcp_rn(1.0f + __expf(-x2))) * x1;
+          cv[j] = __fdividef(x2, 1.0f + __expf(-x2)) * x1;   // as the prefill GEMM1
           float m = fabsf(cv[j]);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
