@@ -163,6 +163,19 @@ def test_router_argument_errors_need_no_gpu():
                                       None) == _lib.MOE_ERR_INVALID_ARG
 
 
+def test_noalloc_route_limits_need_no_gpu():
+    """The no-alloc router: more tokens than its fixed scratch holds give
+    MOE_ERR_TOO_LARGE; an E_global beyond the router's 256 gives MOE_ERR_SHAPE
+    (the shape rules of moe_fp8_forward)."""
+    lib = _lib.load()
+    too_many = lib.moe_fp8_route_noalloc(None, None, 0, 65537, 256, 8, 4, 8, 256, 0, 2.5, None,
+                                         None, None, None)
+    assert too_many == _lib.MOE_ERR_TOO_LARGE
+    wide = lib.moe_fp8_route_noalloc(None, None, 0, 16, 512, 8, 4, 8, 256, 0, 2.5, None, None,
+                                     None, None)
+    assert wide == _lib.MOE_ERR_SHAPE
+
+
 def test_status_strings():
     for code in (0, -1, -2, -3, -4, -5, -6, -7, -8, -9):
         assert _lib.status_string(code) != "unknown status"
