@@ -324,26 +324,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // push them out of L2), and a load issued one K block ahead still
         // stalled every group's first multiply (clock64 traces: ~300 of ~1000
         // cycles per group).
+        // The weight scales are the same for the whole warp: lane i holds K
+        // block 32c + i of the current 32-block chunk c (and of the next), and
+        // each K block takes its value with a shuffle, so the loop issues
+        // their loads once per 32 K blocks instead of twice per K block.
         const float* sa_p = p.a_scale + grow;
+        float w1_c = lane < KB ? __ldg(ws_x1 + lane) : 0.f;
+        float w2_c = lane < KB ? __ldg(ws_x2 + lane) : 0.f;
+        float w1_cn = lane + 32 < KB ? __ldg(ws_x1 + 32 + lane) : 0.f;
+        float w2_cn = lane + 32 < KB ? __ldg(ws_x2 + 32 + lane) : 0.f;
         float sa_n = warp_active ? __ldg(sa_p) : 0.f;
-        float w1_n = __ldg(ws_x1), w2_n = __ldg(ws_x2);
-        float sa_nn = 0.f, w1_nn = 0.f, w2_nn = 0.f;
-        if (KB > 1) {
-          if (warp_active) sa_nn = __ldg(sa_p + p.npad);
-          w1_nn = __ldg(ws_x1 + 1);
-          w2_nn = __ldg(ws_x2 + 1);
-        }
+        float sa_nn = warp_active && KB > 1 ? __ldg(sa_p + p.npad) : 0.f;
         for (int kb = 0; kb < KB; ++kb) {
-          const float s1 = sa_n * w1_n;
-          const float s2 = sa_n * w2_n;
-          sa_n = sa_nn;
-          w1_n = w1_nn;
-          w2_n = w2_nn;
-          if (kb + 2 < KB) {
-            if (warp_active) sa_nn = __ldg(sa_p + static_cast<int64_t>(kb + 2) * p.npad);
-            w1_nn = __ldg(ws_x1 + kb + 2);
-            w2_nn = __ldg(ws_x2 + kb + 2);
+          if ((kb & 31) == 0 && kb > 0) {
+            w1_c = w1_cn;
+            w2_c = w2_cn;
+            const int nk = kb + 32 + lane;
+            w1_cn = nk < KB ? __ldg(ws_x1 + nk) : 0.f;
+            w2_cn = nk < KB ? __ldg(ws_x2 + nk) : 0.f;
           }
+          const float s1 = sa_n * __shfl_sync(0xffffffffu, w1_c, kb & 31);
+          const float s2 = sa_n * __shfl_sync(0xffffffffu, w2_c, kb & 31);
+          sa_n = sa_nn;
+          if (kb + 2 < KB && warp_active) sa_nn = __ldg(sa_p + static_cast<int64_t>(kb + 2) * p.npad);
           const uint32_t buf = g & 1u;
           if (!next_ready && !mbar_wait(&tfull[buf], (g >> 1) & 1u, abort_flag, p.ctrl, 4))
             goto epi_done;
@@ -475,6 +478,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         } else {
         // W2 scale [E, H/128, I/128]: row block 2n + h of this thread's columns.
         const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * kb_rows + 2 * c.n + h) * KB;
+        // Both intermediate scales of K block kb+2 and its weight scale are
+        // loaded at the top of K block kb, two K blocks (four groups) ahead of
+        // their use, as in GEMM1.
         // Both intermediate scales of K block kb+2 and its weight scale are
         // loaded at the top of K block kb, two K blocks (four groups) ahead of
         // their use, as in GEMM1.
