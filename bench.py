@@ -544,7 +544,7 @@ def e2e_run(torch, runner, a):
 
 def prepared_run(torch, shape, inp, fp8_peak, a):
     """The headline workload with the one-time bf16 relayout of W2
-    (``prepare_gemm2_weights``, SURVEY's weight relayout): GEMM2 on bf16
+    (``prepare_gemm2_weights``, a one-time weight relayout): GEMM2 on bf16
     operands without block-scale promotion.  The relayout runs once per layer's
     weights, outside the timed steps; its own time is reported."""
     from moe_b200 import prepare_gemm2_weights

@@ -246,7 +246,7 @@ int moe_fp8_route_noalloc(const float* routing_logits, const void* routing_bias,
  * w2 [E_local, H, I] e4m3, w2_scale [E_local, H/128, I/128] fp32, out
  * [E_local, H, I] bf16 (twice the bytes of w2).  Pass `out` as
  * MoeFwdArgs.gemm2_weights_bf16 to later forwards with the same weights.  No
- * counterpart in the reference (SURVEY's one-time weight relayout).  Asynchronous
+ * counterpart in the reference (a one-time weight relayout).  Asynchronous
  * on `stream`, no allocation; H, I multiples of 128, pointers 16-byte aligned. */
 int moe_fp8_prepare_gemm2_bf16(const void* w2, const float* w2_scale, int64_t E_local, int64_t H,
                                int64_t I, void* out, void* stream);
@@ -255,7 +255,7 @@ int moe_fp8_prepare_gemm2_bf16(const void* w2, const float* w2_scale, int64_t E_
  * logits[T, E] = x[T, H] . w_gate[E, H]^T with bf16 x and w_gate (row-major),
  * products exact in fp32 and fp32 accumulation, fp32 logits [T, E].  The
  * reference receives the logits as an input (kernel.py:562); this op is the
- * step before it (SURVEY's router-GEMM neighbour), with no counterpart there.
+ * step before it (the router GEMM), with no counterpart there.
  * Batches of at most 128 tokens, and shapes with E not a multiple of 256 or H
  * not a multiple of 64, run on CUDA cores in a fixed summation order with every
  * addition rounded to nearest (no workspace needed: pass NULL, 0); larger
