@@ -319,11 +319,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float* ws = p.b_scale + static_cast<int64_t>(c.e) * (2 * ib_rows) * KB;
         const float* ws_x1 = ws + static_cast<int64_t>(c.n) * KB;
         const float* ws_x2 = ws + static_cast<int64_t>(ib_rows + c.n) * KB;
-        // Scales of K block kb+2 are loaded while block kb is promoted: the
-        // permuted activation scales come from DRAM (the permute's row copies
-        // push them out of L2), and a load issued one K block ahead still
-        // stalled every group's first multiply (clock64 traces: ~300 of ~1000
-        // cycles per group).
+        // Activation scales of K block kb+2 are loaded while block kb is
+        // promoted: they come from DRAM (the permute's row copies push them
+        // out of L2), and a load issued one K block ahead stalled every
+        // group's first multiply (clock64 traces: ~300 of ~1000 cycles per
+        // group).
         // The weight scales are the same for the whole warp: lane i holds K
         // block 32c + i of the current 32-block chunk c (and of the next), and
         // each K block takes its value with a shuffle, so the loop issues
@@ -478,9 +478,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         } else {
         // W2 scale [E, H/128, I/128]: row block 2n + h of this thread's columns.
         const float* ws = p.b_scale + (static_cast<int64_t>(c.e) * kb_rows + 2 * c.n + h) * KB;
-        // Both intermediate scales of K block kb+2 and its weight scale are
-        // loaded at the top of K block kb, two K blocks (four groups) ahead of
-        // their use, as in GEMM1.
         // Both intermediate scales of K block kb+2 and its weight scale are
         // loaded at the top of K block kb, two K blocks (four groups) ahead of
         // their use, as in GEMM1.
