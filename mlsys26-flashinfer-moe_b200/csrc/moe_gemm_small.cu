@@ -67,6 +67,8 @@ constexpr int small_smem_bytes() {
   return 1024 + SmallCfg<kMode>::kStages * SmallCfg<kMode>::kStageBytes +
          2 * kSmallScaleFloats * 4 + 4096 + (2 * kMaxBuckets + 2) * 4;
 }
+static_assert(small_smem_bytes<kGemm1>() <= kMaxDynSmemBytes, "decode GEMM1 exceeds shared memory");
+static_assert(small_smem_bytes<kGemm2>() <= kMaxDynSmemBytes, "decode GEMM2 exceeds shared memory");
 
 struct SmallUnit {
   int e, n, row0, nrows;

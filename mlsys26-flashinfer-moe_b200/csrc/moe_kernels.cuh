@@ -212,9 +212,18 @@ int launch_prepare_w2_bf16(const void* w2, const float* w2s, int64_t E, int64_t 
 int launch_quant_1x128(const void* x, int64_t T, int64_t H, void* q, float* scale, int sms,
                        cudaStream_t stream);
 
+// Dynamic shared memory a CTA may opt into on sm_100 (227 KB).
+constexpr int kMaxDynSmemBytes = 232448;
+
 constexpr int gemm_smem_bytes() {
   return 1024 /*alignment slack*/ + kStages * kStageBytes + kXposeBytes +
          4096 /*barriers + tables*/;
 }
+static_assert(gemm_smem_bytes() <= kMaxDynSmemBytes, "GEMM stages exceed shared memory");
+// Barriers (full and empty per stage, two tfull, two tempty, drain, never:
+// 8 B each), TMEM slot and abort words (12 B) and the unit tables (tile_start,
+// counts, skip flag) fit the 4096-byte area.
+static_assert((2 * kStages + 6) * 8 + 12 + (2 * kMaxBuckets + 2) * 4 <= 4096,
+              "GEMM tables exceed their area");
 
 }  // namespace moe
